@@ -1,0 +1,627 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a with fused epilogues (the dense contractions of the
+// PSGD-Kron step: Gram products Q^T Q, term1 = Pg Pg^T, the preconditioner applications P1 G P2, the Q update
+// term1 q, the Procrustes products, and the skinny subspace products V A of the norm lower bounds).
+//
+// CTA layout (192 threads, one CTA per SM):
+//   warp 0        TMA producer: 128x64 A tile and bn x 64 B tile (plus their lo copies in split mode) per stage,
+//                 128-byte swizzled, into a STAGES-deep ring of shared-memory buffers.
+//   warp 1        MMA issuer: one thread issues tcgen05.mma (M = 128, N = bn, K = 16 per instruction) into one
+//                 of two TMEM accumulators; tcgen05.commit releases stages and hands finished accumulators over.
+//   warps 2..5    epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes 32*(w%4)...), the fused
+//                 element-wise transform, stores, and deterministic per-tile reductions.
+// Two accumulators let the epilogue of tile i overlap the MMAs of tile i+1. Every wait is bounded in time.
+#include "common.cuh"
+#include "psgd_b200.h"
+
+#include <float.h>
+#include <stdio.h>
+#include <string.h>
+#include <vector>
+
+namespace psgd {
+
+constexpr int BM = 128, BK = 64;
+constexpr int GEMM_THREADS = 192;
+
+struct __align__(64) GemmDesc {
+  CUtensorMap ta[2];  // A hi, lo
+  CUtensorMap tb[2];  // B hi, lo
+  PsgdGemmSpec s;
+  int tiles_m, tiles_n;
+};
+
+template <int SPLIT, int BNMAX, int STAGES>
+struct GemmCfg {
+  static constexpr int NOPS = SPLIT == 1 ? 1 : 2;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BNMAX * BK * 2;
+  static constexpr int STAGE_BYTES = NOPS * (A_BYTES + B_BYTES);
+  static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int TMEM_COLS = 2 * BNMAX;
+  static constexpr int CTRL_BYTES = 256;  // barriers, TMEM slot, abort flag
+  static constexpr int RED_FLOATS = 4 * BNMAX + BNMAX + 32;
+  static constexpr int SMEM_BYTES = 1024 + TILE_BYTES + CTRL_BYTES + RED_FLOATS * 4;
+  static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
+};
+
+// ---- epilogue ------------------------------------------------------------------------------------------------
+// Stores `w` consecutive fp32 values of one row, vectorised when the run is 16-byte aligned and in range.
+PSGD_DEVI void store_row_f32(float* dst, const float* v, int w, int nvalid) {
+  if (nvalid == w && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4)
+      if (j < w) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+  } else {
+    for (int j = 0; j < nvalid; ++j) dst[j] = v[j];
+  }
+}
+
+PSGD_DEVI void store_row_bf16(__nv_bfloat16* hi, __nv_bfloat16* lo, const float* v, int w, int nvalid) {
+  if (nvalid == w && ((reinterpret_cast<uintptr_t>(hi) & 15) == 0) &&
+      (lo == nullptr || (reinterpret_cast<uintptr_t>(lo) & 15) == 0)) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      if (j < w) {
+        __align__(16) __nv_bfloat16 h[8], l[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) split_bf16(v[j + u], h[u], l[u]);
+        *reinterpret_cast<uint4*>(hi + j) = *reinterpret_cast<const uint4*>(h);
+        if (lo) *reinterpret_cast<uint4*>(lo + j) = *reinterpret_cast<const uint4*>(l);
+      }
+    }
+  } else {
+    for (int j = 0; j < nvalid; ++j) {
+      __nv_bfloat16 h, l;
+      split_bf16(v[j], h, l);
+      hi[j] = h;
+      if (lo) lo[j] = l;
+    }
+  }
+}
+
+template <int BNMAX>
+__device__ void epilogue_tile(const GemmDesc& d, int tm, int tn, uint32_t tacc, int q, int lane, float* red,
+                              float* cs, float* misc) {
+  const PsgdGemmSpec& s = d.s;
+  const int bn = s.bn;
+  const int r = q * 32 + lane;  // tile row held by this thread (TMEM lane)
+  const long long m0 = (long long)tm * BM, n0 = (long long)tn * bn;
+  const long long gr = m0 + r;
+  const bool rvalid = gr < s.M;
+  const int et = r;  // 0..127 among the epilogue threads
+  const bool syrk = s.mode == PSGD_GEMM_SYRK;
+  const bool diag_tile = syrk && tm == tn;
+
+  const float alpha = s.alpha * (s.alpha_ptr ? __ldg(s.alpha_ptr) : 1.f);
+  const float beta = s.beta * (s.beta_ptr ? __ldg(s.beta_ptr) : 1.f);
+  const float rsc = (s.row_scale && rvalid) ? s.row_scale[gr] : 1.f;
+  const bool has_cs = s.col_scale != nullptr || s.cs_mode != 0;
+  if (has_cs) {
+    for (int c = et; c < bn; c += 128) {
+      const long long gc = n0 + c;
+      float v = 1.f;
+      if (gc < s.N) {
+        if (s.col_scale) {
+          v = s.col_scale[gc];
+        } else {
+          const float nf = *s.cs_nf;
+          if (s.cs_mode == 1) {
+            v = 1.f / nf;
+          } else {
+            float acc = 0.f;
+            for (int t = 0; t < s.cs_T; ++t) acc += s.cs_part[(long long)t * s.N + gc];
+            v = 1.f / (nf * (sqrtf(acc) + FLT_MIN));
+          }
+        }
+      }
+      cs[c] = v;
+    }
+  }
+  const bool need_col = s.part_col != nullptr || (syrk && s.part_row != nullptr);
+  named_sync(1, 128);
+
+  float tsum = 0.f, rsum = 0.f, dsum = 0.f;
+  for (int c0 = 0; c0 < bn; c0 += 32) {
+    float v[32];
+    const int w = (bn - c0) >= 32 ? 32 : 16;
+    if (w == 32) {
+      tmem_ld32(tacc + (uint32_t)c0, v);
+    } else {
+      tmem_ld16(tacc + (uint32_t)c0, v);
+#pragma unroll
+      for (int j = 16; j < 32; ++j) v[j] = 0.f;
+    }
+    const long long gc0 = n0 + c0;
+    int nvalid = 0;  // valid columns of this row in the chunk
+    if (rvalid) nvalid = (int)max(0LL, min((long long)w, (long long)s.N - gc0));
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j < nvalid) {
+        float x = v[j] * alpha;
+        if (s.aux) x += beta * s.aux[gr * s.ld_aux + gc0 + j];
+        x *= rsc;
+        if (has_cs) x *= cs[c0 + j];
+        v[j] = x;
+      } else {
+        v[j] = 0.f;
+      }
+    }
+
+    if (!syrk) {
+      if (nvalid > 0) {
+        if (s.out_f32) store_row_f32(s.out_f32 + gr * s.ld_f32 + gc0, v, w, nvalid);
+        if (s.out_hi)
+          store_row_bf16((__nv_bfloat16*)s.out_hi + gr * s.ld_b + gc0,
+                         s.out_lo ? (__nv_bfloat16*)s.out_lo + gr * s.ld_b + gc0 : nullptr, v, w, nvalid);
+      }
+      if (s.out_hi_t) {  // transposed: consecutive lanes write consecutive rows (coalesced)
+        __nv_bfloat16* ht = (__nv_bfloat16*)s.out_hi_t;
+        __nv_bfloat16* lt = (__nv_bfloat16*)s.out_lo_t;
+        for (int j = 0; j < w; ++j) {
+          if (j < nvalid) {
+            __nv_bfloat16 h, l;
+            split_bf16(v[j], h, l);
+            ht[(gc0 + j) * s.ld_bt + gr] = h;
+            if (lt) lt[(gc0 + j) * s.ld_bt + gr] = l;
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        tsum += v[j] * v[j];
+        rsum += v[j] * v[j];
+      }
+      if (s.part_col) {
+        float sq[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sq[j] = v[j] * v[j];
+        red[q * BNMAX + c0 + lane] = warp_colsum32(sq, lane);
+      }
+    } else {
+      // symmetric output: (gr, gc) for gc >= gr and its mirror (gc, gr) for gc > gr
+      for (int j = 0; j < nvalid; ++j) {
+        const long long gc = gc0 + j;
+        if (gc < gr) continue;
+        __nv_bfloat16 h, l;
+        split_bf16(v[j], h, l);
+        if (s.out_f32) s.out_f32[gr * s.ld_f32 + gc] = v[j];
+        if (s.out_hi) ((__nv_bfloat16*)s.out_hi)[gr * s.ld_b + gc] = h;
+        if (s.out_lo) ((__nv_bfloat16*)s.out_lo)[gr * s.ld_b + gc] = l;
+        if (gc > gr) {
+          if (s.out_f32) s.out_f32[gc * s.ld_f32 + gr] = v[j];
+          if (s.out_hi) ((__nv_bfloat16*)s.out_hi)[gc * s.ld_b + gr] = h;
+          if (s.out_lo) ((__nv_bfloat16*)s.out_lo)[gc * s.ld_b + gr] = l;
+        }
+        if (s.diag_out && gc == gr) s.diag_out[gr] = v[j];
+        if (s.dot_aux) {
+          float dd = s.dot_aux[gr * s.ld_dot + gc];
+          if (gc > gr) dd += s.dot_aux[gc * s.ld_dot + gr];
+          dsum += v[j] * dd;
+        }
+      }
+      float sq[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const long long gc = gc0 + j;
+        const float x2 = v[j] * v[j];
+        rsum += (gc >= gr) ? x2 : 0.f;
+        sq[j] = (gc > gr) ? x2 : 0.f;
+      }
+      if (need_col) red[q * BNMAX + c0 + lane] = warp_colsum32(sq, lane);
+    }
+  }
+
+  // ---- reductions over the 128 epilogue threads (fixed order) ----
+  if (s.part_tile || s.part_dot) {
+    const float t1 = warp_sum(tsum), t2 = warp_sum(dsum);
+    if (lane == 0) {
+      misc[q] = t1;
+      misc[4 + q] = t2;
+    }
+  }
+  named_sync(1, 128);
+  const long long tile_lin = (long long)tm * d.tiles_n + tn;
+  if (et == 0) {
+    if (s.part_tile) s.part_tile[tile_lin] = ((misc[0] + misc[1]) + misc[2]) + misc[3];
+    if (s.part_dot) s.part_dot[tile_lin] = ((misc[4] + misc[5]) + misc[6]) + misc[7];
+  }
+  if (!syrk) {
+    if (s.part_row && rvalid) s.part_row[(long long)tn * s.M + gr] = rsum;
+    if (s.part_col) {
+      for (int c = et; c < bn; c += 128) {
+        const long long gc = n0 + c;
+        if (gc < s.N) {
+          const float t = ((red[c] + red[BNMAX + c]) + red[2 * BNMAX + c]) + red[3 * BNMAX + c];
+          s.part_col[(long long)tm * s.N + gc] = t;
+        }
+      }
+    }
+  } else if (s.part_row) {
+    // column sums of the strict upper part are the mirrored rows' contributions
+    const int c = et;
+    const float colsum = ((red[c] + red[BNMAX + c]) + red[2 * BNMAX + c]) + red[3 * BNMAX + c];
+    if (diag_tile) {
+      if (rvalid) s.part_row[(long long)tn * s.M + gr] = rsum + colsum;
+    } else {
+      if (rvalid) s.part_row[(long long)tn * s.M + gr] = rsum;
+      const long long gc = n0 + c;
+      if (gc < s.N) s.part_row[(long long)tm * s.M + gc] = colsum;
+    }
+  }
+  named_sync(1, 128);  // red/cs/misc are reused by the next tile
+}
+
+// Tile t of a launch: from the explicit list (grouped launch) or, with no list, the t-th tile of problem 0 in
+// row-major order (upper tiles only for SYRK).
+PSGD_DEVI void get_tile(const GemmDesc* descs, const uint32_t* tiles, int t, int& p, int& tm, int& tn) {
+  if (tiles) {
+    p = (int)tiles[2 * t];
+    tm = (int)(tiles[2 * t + 1] >> 16);
+    tn = (int)(tiles[2 * t + 1] & 0xFFFF);
+    return;
+  }
+  p = 0;
+  const GemmDesc& d = descs[0];
+  if (d.s.mode == PSGD_GEMM_SYRK) {
+    int row = 0, rem = t;
+    while (rem >= d.tiles_n - row) {
+      rem -= d.tiles_n - row;
+      ++row;
+    }
+    tm = row;
+    tn = row + rem;
+  } else {
+    tm = t / d.tiles_n;
+    tn = t % d.tiles_n;
+  }
+}
+
+// ---- the kernel body ------------------------------------------------------------------------------------------
+template <int SPLIT, int BNMAX, int STAGES>
+__device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, const uint32_t* __restrict__ tiles,
+                                          int ntiles, int* err) {
+  using C = GemmCfg<SPLIT, BNMAX, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::TILE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* red = reinterpret_cast<float*>(smem + C::TILE_BYTES + C::CTRL_BYTES);
+  float* cs = red + 4 * BNMAX;
+  float* misc = cs + BNMAX;
+  volatile int* epi_ok = reinterpret_cast<volatile int*>(misc + 16);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    mbar_init(drain, 1);
+    *abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    __syncwarp();
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      uint32_t g = 0;
+      uint32_t armed[STAGES];  // phases armed per stage, to drain in-flight copies on abort
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) armed[s] = 0;
+      for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x) {
+        int p, tm, tn;
+        get_tile(descs, tiles, t, p, tm, tn);
+        const GemmDesc& d = descs[p];
+        const int nk = (d.s.K + BK - 1) / BK;
+        const uint32_t bytes = C::NOPS * (C::A_BYTES + d.s.bn * BK * 2);
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % STAGES;
+          const uint32_t ph = (g / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort)) break;
+          mbar_arrive_expect_tx(&full[s], bytes);
+          armed[s] += 1;
+          uint8_t* sa = smem + s * C::STAGE_BYTES;
+          uint8_t* sb = sa + C::NOPS * C::A_BYTES;
+          tma_load_2d(sa, &d.ta[0], &full[s], kb * BK, tm * BM);
+          tma_load_2d(sb, &d.tb[0], &full[s], kb * BK, tn * d.s.bn);
+          if (SPLIT != 1) {
+            tma_load_2d(sa + C::A_BYTES, &d.ta[1], &full[s], kb * BK, tm * BM);
+            tma_load_2d(sb + C::B_BYTES, &d.tb[1], &full[s], kb * BK, tn * d.s.bn);
+          }
+        }
+      }
+      if (*abort) {  // let every armed copy land before the CTA releases its shared memory
+        for (int s = 0; s < STAGES; ++s) {
+          if (armed[s] == 0) continue;
+          volatile int never = 0;
+          mbar_wait(&full[s], (armed[s] - 1) & 1, &never);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      uint32_t g = 0, i = 0;
+      bool issued = false;
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+        int p, tm, tn;
+        get_tile(descs, tiles, t, p, tm, tn);
+        const GemmDesc& d = descs[p];
+        const int nk = (d.s.K + BK - 1) / BK;
+        const int bn = d.s.bn;
+        const uint32_t acc = i & 1, aph = (i >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], aph ^ 1, abort)) break;
+        tc_fence_after();
+        const uint32_t dt = tmem_base + acc * BNMAX;
+        const uint32_t idesc = idesc_bf16_m128(bn);
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % STAGES;
+          const uint32_t ph = (g / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_hi = smem_u32(smem + s * C::STAGE_BYTES);
+          const uint32_t b_hi = a_hi + C::NOPS * C::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = sdesc_k_sw128(a_hi + kk * 32), bd = sdesc_k_sw128(b_hi + kk * 32);
+            umma_bf16(dt, ad, bd, idesc, (kb | kk) != 0);
+            if (SPLIT != 1) {
+              umma_bf16(dt, ad, sdesc_k_sw128(b_hi + C::B_BYTES + kk * 32), idesc, 1);
+              umma_bf16(dt, sdesc_k_sw128(a_hi + C::A_BYTES + kk * 32), bd, idesc, 1);
+            }
+          }
+          issued = true;
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+      }
+      if (*abort && issued) {  // every issued MMA must finish before TMEM and shared memory are released
+        umma_commit(drain);
+        volatile int never = 0;
+        mbar_wait(drain, 0, &never);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;
+    uint32_t i = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+      int p, tm, tn;
+      get_tile(descs, tiles, t, p, tm, tn);
+      const GemmDesc& d = descs[p];
+      const uint32_t acc = i & 1, aph = (i >> 1) & 1;
+      // the four epilogue warps agree on success before any named barrier, so none can be left waiting there
+      const bool ok = mbar_wait(&tfull[acc], aph, abort);
+      if (lane == 0) epi_ok[q] = ok ? 1 : 0;
+      named_sync(1, 128);
+      const bool all_ok = epi_ok[0] && epi_ok[1] && epi_ok[2] && epi_ok[3];
+      named_sync(1, 128);
+      if (!all_ok) break;
+      tc_fence_after();
+      const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BNMAX;
+      epilogue_tile<BNMAX>(d, tm, tn, tacc, q, lane, red, cs, misc);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+  if (threadIdx.x == 0 && *abort) atomicOr(err, ERR_TIMEOUT_FULL);
+}
+
+template <int SPLIT, int BNMAX, int STAGES>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_group_kernel(const GemmDesc* __restrict__ descs, const uint32_t* __restrict__ tiles, int ntiles, int* err) {
+  gemm_body<SPLIT, BNMAX, STAGES>(descs, tiles, ntiles, err);
+}
+
+// Single problem: the descriptor is a __grid_constant__ parameter and the tile list is implicit.
+template <int SPLIT, int BNMAX, int STAGES>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_single_kernel(const __grid_constant__ GemmDesc desc, const uint32_t* __restrict__ tiles, int ntiles,
+                       int* err) {
+  gemm_body<SPLIT, BNMAX, STAGES>(&desc, tiles, ntiles, err);
+}
+
+// ---- host side --------------------------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;  // resolved once; the driver entry point never changes
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// bf16 row-major matrix (rows x cols, leading dimension ld) as TMA tiles of box_rows x 64, 128-byte swizzled.
+static int encode_bf16(CUtensorMap* tm, const void* ptr, int rows, int cols, long long ld, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return PSGD_ETMAP;
+  if (ptr == nullptr || (reinterpret_cast<uintptr_t>(ptr) & 15) || (ld % 8) || ld < cols || rows < 1 || cols < 1)
+    return PSGD_EINVAL;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? PSGD_OK : PSGD_ETMAP;
+}
+
+static bool valid_bn(int bn, int split) {
+  const int bnmax = split == 1 ? 256 : 128;
+  return (bn == 16 || bn == 32 || bn == 64 || bn == 128 || bn == 256) && bn <= bnmax;
+}
+
+static int check_spec(const PsgdGemmSpec& s, int split) {
+  if (split != 1 && split != 3) return PSGD_EINVAL;
+  if (s.M < 1 || s.N < 1 || s.K < 1 || !valid_bn(s.bn, split)) return PSGD_EINVAL;
+  if (split == 3 && (s.a_lo == nullptr || s.b_lo == nullptr)) return PSGD_EINVAL;
+  if (s.mode == PSGD_GEMM_SYRK && (s.M != s.N || s.bn != 128)) return PSGD_EINVAL;
+  if (s.mode != PSGD_GEMM_PLAIN && s.mode != PSGD_GEMM_SYRK) return PSGD_EINVAL;
+  if (s.cs_mode && (s.cs_nf == nullptr || (s.cs_mode == 2 && (s.cs_part == nullptr || s.cs_T < 1)))) return PSGD_EINVAL;
+  if (s.M > 65535 * BM || s.N > 65535 * s.bn) return PSGD_EINVAL;
+  return PSGD_OK;
+}
+
+static int fill_desc(GemmDesc* d, const PsgdGemmSpec& s, int split) {
+  int rc = check_spec(s, split);
+  if (rc) return rc;
+  memset(d, 0, sizeof(GemmDesc));
+  d->s = s;
+  d->tiles_m = (s.M + BM - 1) / BM;
+  d->tiles_n = (s.N + s.bn - 1) / s.bn;
+  if ((rc = encode_bf16(&d->ta[0], s.a_hi, s.M, s.K, s.lda, BM))) return rc;
+  if ((rc = encode_bf16(&d->tb[0], s.b_hi, s.N, s.K, s.ldb, s.bn))) return rc;
+  if (split != 1) {
+    if ((rc = encode_bf16(&d->ta[1], s.a_lo, s.M, s.K, s.lda, BM))) return rc;
+    if ((rc = encode_bf16(&d->tb[1], s.b_lo, s.N, s.K, s.ldb, s.bn))) return rc;
+  } else {
+    d->ta[1] = d->ta[0];
+    d->tb[1] = d->tb[0];
+  }
+  return PSGD_OK;
+}
+
+static int spec_tiles(const PsgdGemmSpec& s) {
+  const int tmn = (s.M + BM - 1) / BM, tnn = (s.N + s.bn - 1) / s.bn;
+  if (s.mode == PSGD_GEMM_SYRK) return tmn * (tmn + 1) / 2;
+  return tmn * tnn;
+}
+
+static void append_tiles(const PsgdGemmSpec& s, uint32_t p, uint32_t* out, int& k) {
+  const int tmn = (s.M + BM - 1) / BM, tnn = (s.N + s.bn - 1) / s.bn;
+  for (int tm = 0; tm < tmn; ++tm)
+    for (int tn = (s.mode == PSGD_GEMM_SYRK ? tm : 0); tn < tnn; ++tn) {
+      out[2 * k] = p;
+      out[2 * k + 1] = ((uint32_t)tm << 16) | (uint32_t)tn;
+      ++k;
+    }
+}
+
+static int num_sms() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  return n;
+}
+
+template <int SPLIT, int BNMAX, int STAGES>
+static int launch_group(const GemmDesc* descs, const uint32_t* tiles, int ntiles, int* err, cudaStream_t st) {
+  using C = GemmCfg<SPLIT, BNMAX, STAGES>;
+  auto k = gemm_group_kernel<SPLIT, BNMAX, STAGES>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
+    return PSGD_ELAUNCH;
+  const int grid = ntiles < num_sms() ? ntiles : num_sms();
+  k<<<grid, GEMM_THREADS, C::SMEM_BYTES, st>>>(descs, tiles, ntiles, err);
+  return cudaGetLastError() == cudaSuccess ? PSGD_OK : PSGD_ELAUNCH;
+}
+
+template <int SPLIT, int BNMAX, int STAGES>
+static int launch_single(const GemmDesc& desc, const uint32_t* tiles, int ntiles, int* err, cudaStream_t st) {
+  using C = GemmCfg<SPLIT, BNMAX, STAGES>;
+  auto k = gemm_single_kernel<SPLIT, BNMAX, STAGES>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
+    return PSGD_ELAUNCH;
+  const int grid = ntiles < num_sms() ? ntiles : num_sms();
+  k<<<grid, GEMM_THREADS, C::SMEM_BYTES, st>>>(desc, tiles, ntiles, err);
+  return cudaGetLastError() == cudaSuccess ? PSGD_OK : PSGD_ELAUNCH;
+}
+
+}  // namespace psgd
+
+using namespace psgd;
+
+extern "C" int psgd_num_sms(void) { return num_sms(); }
+
+extern "C" size_t psgd_gemm_table_bytes(int nspecs) { return (size_t)(nspecs > 0 ? nspecs : 0) * sizeof(GemmDesc); }
+
+extern "C" int psgd_gemm_count_tiles(const PsgdGemmSpec* specs, int nspecs) {
+  if (!specs || nspecs < 0) return PSGD_EINVAL;
+  long long n = 0;
+  for (int i = 0; i < nspecs; ++i) {
+    if (specs[i].M < 1 || specs[i].N < 1 || !valid_bn(specs[i].bn, 1)) return PSGD_EINVAL;
+    n += spec_tiles(specs[i]);
+  }
+  return n > 0x7fffffff ? PSGD_EINVAL : (int)n;
+}
+
+extern "C" int psgd_gemm_encode(const PsgdGemmSpec* specs, int nspecs, void* host_table, size_t table_bytes,
+                                uint32_t* host_tiles, int max_tiles, int* ntiles) {
+  if (!specs || nspecs < 1 || !host_table || !host_tiles || !ntiles) return PSGD_EINVAL;
+  if (table_bytes < psgd_gemm_table_bytes(nspecs) || (reinterpret_cast<uintptr_t>(host_table) & 63)) return PSGD_ESPACE;
+  if (nspecs > 65535) return PSGD_EINVAL;
+  const int need = psgd_gemm_count_tiles(specs, nspecs);
+  if (need < 0) return need;
+  if (need > max_tiles) return PSGD_ESPACE;
+  GemmDesc* descs = reinterpret_cast<GemmDesc*>(host_table);
+  // split is a launch-time choice; encode the lo maps whenever lo pointers are present
+  for (int i = 0; i < nspecs; ++i) {
+    const int split = (specs[i].a_lo && specs[i].b_lo) ? 3 : 1;
+    const int rc = fill_desc(&descs[i], specs[i], split == 3 && specs[i].bn > 128 ? 1 : split);
+    if (rc) return rc;
+  }
+  int k = 0;
+  for (int i = 0; i < nspecs; ++i) append_tiles(specs[i], (uint32_t)i, host_tiles, k);
+  *ntiles = k;
+  return PSGD_OK;
+}
+
+extern "C" int psgd_gemm_launch(const void* dev_table, const uint32_t* dev_tiles, int ntiles, int split, int* dev_err,
+                                cudaStream_t stream) {
+  if (!dev_table || !dev_tiles || ntiles < 0 || !dev_err) return PSGD_EINVAL;
+  if (ntiles == 0) return PSGD_OK;
+  const GemmDesc* d = reinterpret_cast<const GemmDesc*>(dev_table);
+  if (split == 1) return launch_group<1, 256, 4>(d, dev_tiles, ntiles, dev_err, stream);
+  if (split == 3) return launch_group<3, 128, 3>(d, dev_tiles, ntiles, dev_err, stream);
+  return PSGD_EINVAL;
+}
+
+extern "C" int psgd_gemm(const PsgdGemmSpec* spec, int split, int* dev_err, cudaStream_t stream) {
+  if (!spec || !dev_err) return PSGD_EINVAL;
+  GemmDesc desc;
+  int rc = fill_desc(&desc, *spec, split);
+  if (rc) return rc;
+  const int nt = spec_tiles(*spec);
+  if (split == 1) return launch_single<1, 256, 4>(desc, nullptr, nt, dev_err, stream);
+  return launch_single<3, 128, 3>(desc, nullptr, nt, dev_err, stream);
+}

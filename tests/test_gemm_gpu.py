@@ -1,0 +1,168 @@
+"""tcgen05 GEMM (libpsgd_b200.so, psgd_gemm / psgd_gemm_launch) against plain PyTorch fp32/fp64 products of the
+same operands: plain and split (hi/lo) arithmetic, SYRK with mirrored output, the fused epilogue terms and
+reductions, and grouped launches over problems of different shapes."""
+import pytest
+import torch
+
+from psgd_pro_b200 import kernels as K
+
+pytestmark = pytest.mark.gpu
+
+
+def rel(a, b):
+    return ((a.double() - b.double()).norm() / b.double().norm().clamp_min(1e-30)).item()
+
+
+def bf16_operand(rows, cols, dev, gen, split=False, scale=1.0):
+    x = torch.randn(rows, cols, generator=gen, device="cpu").mul_(scale).to(dev)
+    hi, lo = K.operand(rows, cols, dev, split=split)
+    K.split_into(x, hi, lo)
+    return x, (hi, lo)
+
+
+def err_word(dev):
+    return torch.zeros(1, dtype=torch.int32, device=dev)
+
+
+@pytest.mark.parametrize("M,N,Kd,bn", [(128, 128, 64, 128), (256, 512, 1024, 256), (200, 72, 100, 64),
+                                       (1, 16, 8, 16), (300, 33, 70, 32), (130, 260, 129, 256)])
+def test_plain_bf16(cuda, M, N, Kd, bn):
+    g = torch.Generator().manual_seed(M * 7 + N)
+    a, A = bf16_operand(M, Kd, cuda, g)
+    b, B = bf16_operand(N, Kd, cuda, g)
+    out = torch.full((M, N), float("nan"), device=cuda)
+    err = err_word(cuda)
+    K.gemm(K.make_spec(A, B, M, N, Kd, bn=bn, out_f32=out), 1, err)
+    ref = A[0][:, :Kd].float() @ B[0][:, :Kd].float().T
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    assert rel(out, ref) < 1e-5
+
+
+@pytest.mark.parametrize("M,N,Kd,bn", [(256, 256, 512, 128), (192, 576, 192, 64), (65, 10, 65, 16)])
+def test_split_fp32(cuda, M, N, Kd, bn):
+    g = torch.Generator().manual_seed(3)
+    a, A = bf16_operand(M, Kd, cuda, g, split=True)
+    b, B = bf16_operand(N, Kd, cuda, g, split=True)
+    out = torch.empty(M, N, device=cuda)
+    err = err_word(cuda)
+    K.gemm(K.make_spec(A, B, M, N, Kd, bn=bn, out_f32=out), 3, err)
+    ref = a.double() @ b.double().T
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    assert rel(out, ref) < 2e-5, rel(out, ref)
+    # single-pass bf16 is visibly worse on the same inputs (the split is doing work)
+    out1 = torch.empty(M, N, device=cuda)
+    K.gemm(K.make_spec(A, B, M, N, Kd, bn=bn, out_f32=out1), 1, err)
+    assert rel(out1, ref) > 10 * rel(out, ref)
+
+
+@pytest.mark.parametrize("n,Kd,split", [(128, 64, 1), (384, 200, 3), (300, 1000, 1), (10, 7, 3)])
+def test_syrk_symmetric(cuda, n, Kd, split):
+    g = torch.Generator().manual_seed(n)
+    x, X = bf16_operand(n, Kd, cuda, g, split=split == 3)
+    T = (n + 127) // 128
+    out = torch.full((n, n), float("nan"), device=cuda)
+    hi, lo = K.operand(n, n, cuda, split=split == 3)
+    part_row = torch.full((T, n), float("nan"), device=cuda)
+    diag = torch.empty(n, device=cuda)
+    dot_aux = torch.randn(n, n, generator=g).to(cuda)
+    part_dot = torch.zeros(T * T, device=cuda)
+    err = err_word(cuda)
+    spec = K.make_spec(X, X, n, n, Kd, bn=128, mode=K.PSGD_GEMM_SYRK, out_f32=out, out_hi=hi, out_lo=lo,
+                       part_row=part_row, diag_out=diag, dot_aux=dot_aux, part_dot=part_dot)
+    K.gemm(spec, split, err)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    xs = x.double() if split == 3 else X[0][:, :Kd].double()
+    ref = xs @ xs.T
+    assert torch.equal(out, out.T)  # exactly symmetric
+    assert rel(out, ref) < (2e-5 if split == 3 else 1e-5)
+    assert rel(hi[:, :n].float(), ref) < 1e-2
+    assert rel(part_row.sum(0), (ref ** 2).sum(1)) < 1e-4
+    assert rel(diag, ref.diagonal()) < 2e-5
+    got_dot = sum(part_dot[tm * T + tn].item() for tm in range(T) for tn in range(tm, T))
+    want = (ref * dot_aux.double()).sum().item()
+    assert abs(got_dot - want) <= 1e-4 * (ref.abs() * dot_aux.double().abs()).sum().item()
+
+
+def test_epilogue_terms(cuda):
+    g = torch.Generator().manual_seed(11)
+    M, N, Kd = 260, 96, 130
+    a, A = bf16_operand(M, Kd, cuda, g, split=True)
+    b, B = bf16_operand(N, Kd, cuda, g, split=True)
+    aux = torch.randn(M, N, generator=g).to(cuda)
+    rs = torch.rand(M, generator=g).to(cuda) + 0.5
+    csv = torch.rand(N, generator=g).to(cuda) + 0.5
+    ap = torch.tensor([0.25], device=cuda)
+    bp = torch.tensor([2.0], device=cuda)
+    out = torch.empty(M, N, device=cuda)
+    hi_t, lo_t = K.operand(N, M, cuda, split=True)
+    tm_n, tn_n = (M + 127) // 128, (N + 31) // 32
+    part_tile = torch.zeros(tm_n * tn_n, device=cuda)
+    part_col = torch.zeros(tm_n, N, device=cuda)
+    part_row = torch.zeros(tn_n, M, device=cuda)
+    err = err_word(cuda)
+    spec = K.make_spec(A, B, M, N, Kd, bn=32, alpha=-3.0, beta=0.5, alpha_ptr=ap, beta_ptr=bp, aux=aux, row_scale=rs,
+                       col_scale=csv, out_f32=out, out_hi_t=hi_t, out_lo_t=lo_t, part_tile=part_tile,
+                       part_col=part_col, part_row=part_row)
+    K.gemm(spec, 3, err)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    ref = ((-0.75) * (a.double() @ b.double().T) + 1.0 * aux.double()) * rs.double()[:, None] * csv.double()[None, :]
+    assert rel(out, ref) < 2e-5
+    assert rel(hi_t[:, :M].float() + lo_t[:, :M].float(), ref.T) < 2e-5
+    assert rel(part_tile.sum(), (ref ** 2).sum()) < 1e-5
+    assert rel(part_col.sum(0), (ref ** 2).sum(0)) < 1e-5
+    assert rel(part_row.sum(0), (ref ** 2).sum(1)) < 1e-5
+
+
+def test_col_scale_from_partials(cuda):
+    """cs_mode 2: column c scaled by 1 / (nf (||prev_c|| + tiny)) from a previous product's column partials."""
+    g = torch.Generator().manual_seed(5)
+    M, N, Kd = 384, 32, 384
+    a, A = bf16_operand(M, Kd, cuda, g)
+    b, B = bf16_operand(N, Kd, cuda, g)
+    T = 3
+    parts = torch.rand(T, N, generator=g).to(cuda)
+    nf = torch.tensor([1.7], device=cuda)
+    out = torch.empty(M, N, device=cuda)
+    err = err_word(cuda)
+    K.gemm(K.make_spec(A, B, M, N, Kd, bn=32, out_f32=out, cs_part=parts, cs_T=T, cs_mode=2, cs_nf=nf), 1, err)
+    torch.cuda.synchronize()
+    sc = 1.0 / (1.7 * (parts.double().sum(0).sqrt() + torch.finfo(torch.float32).tiny))
+    ref = (A[0][:, :Kd].double() @ B[0][:, :Kd].double().T) * sc[None, :]
+    assert rel(out, ref) < 1e-5
+
+
+@pytest.mark.parametrize("split", [1, 3])
+def test_group_launch(cuda, split):
+    g = torch.Generator().manual_seed(17)
+    shapes = [(512, 512, 512, 128), (64, 10, 64, 16), (300, 700, 90, 64), (1024, 256, 256, 128), (8, 8, 8, 16)]
+    if split == 1:
+        shapes.append((640, 512, 320, 256))
+    specs, refs, outs, keep = [], [], [], []
+    for (M, N, Kd, bn) in shapes:
+        a, A = bf16_operand(M, Kd, cuda, g, split=split == 3)
+        b, B = bf16_operand(N, Kd, cuda, g, split=split == 3)
+        keep += [A, B]  # specs hold raw device pointers: the operands must outlive the launches
+        out = torch.empty(M, N, device=cuda)
+        specs.append(K.make_spec(A, B, M, N, Kd, bn=bn, out_f32=out))
+        outs.append(out)
+        refs.append(a.double() @ b.double().T if split == 3 else A[0][:, :Kd].double() @ B[0][:, :Kd].double().T)
+    n = 48
+    x, X = bf16_operand(n, 100, cuda, g, split=split == 3)
+    sy = torch.empty(n, n, device=cuda)
+    specs.append(K.make_spec(X, X, n, n, 100, bn=128, mode=K.PSGD_GEMM_SYRK, out_f32=sy))
+    xs = x.double() if split == 3 else X[0][:, :100].double()
+    outs.append(sy)
+    refs.append(xs @ xs.T)
+    keep.append(X)
+    grp = K.GemmGroup(specs, split, cuda, keep=keep)
+    err = err_word(cuda)
+    for _ in range(3):  # relaunch: same results
+        grp.launch(err)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    for o, r in zip(outs, refs):
+        assert rel(o, r) < (2e-5 if split == 3 else 1e-5)
