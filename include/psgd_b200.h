@@ -35,8 +35,9 @@ extern "C" {
  *   value(r, c)  = alpha' * D[r, c] + beta' * aux[r, c]       (aux term only when aux != NULL)
  *                  then * row_scale[r] * colscale[c]           (when given)
  *   alpha' = alpha * (*alpha_ptr if alpha_ptr), beta' likewise (device scalars, read at run time).
- *   colscale[c] = col_scale[c], or from cs_mode: 1 -> 1 / *cs_nf;
- *                 2 -> 1 / (*cs_nf * (sqrt(sum_t cs_part[t * N + c]) + FLT_MIN))   (t < cs_T)
+ *   colscale[c] = col_scale[c], or from cs_mode (the subspace products of the norm lower bounds):
+ *                 1 -> value / *cs_nf;  2 -> (value / (sqrt(sum_t cs_part[t * N + c]) + FLT_MIN)) / *cs_nf
+ *                 (t < cs_T), the two divisions applied in this order
  * Outputs (each optional): out_f32 (r, c) fp32; out_hi/out_lo (r, c) bf16; out_hi_t/out_lo_t (c, r) bf16.
  * Reductions (each optional, deterministic, one slot per tile, no atomics):
  *   part_tile[tm * tiles_n + tn] = sum value^2 over the tile
@@ -86,6 +87,118 @@ int psgd_gemm_launch(const void* dev_table, const uint32_t* dev_tiles, int ntile
 
 /* Number of SMs the grouped launches use on the current device (grid size of the persistent kernels). */
 int psgd_num_sms(void);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * Memory-bound step kernels. Each takes a device array of items (one per parameter or factor, encoded by the
+ * caller), an optional device work list of (item, tile) pairs (uint32 pairs: item index, (ti << 16) | tj),
+ * the device hyper-parameter vector and the device error word. Sums are deterministic: fixed-order partials,
+ * no atomics. Hyper-parameter slots (float hyper[PSGD_HY_COUNT]): */
+#define PSGD_HY_LR_PRECOND 0   /* lr_preconditioner */
+#define PSGD_HY_BETA_L 1       /* betaL */
+#define PSGD_HY_DAMPING 2      /* damping */
+#define PSGD_HY_LR_PARAMS 3    /* lr_params */
+#define PSGD_HY_MAX_AVG 4      /* grad_clip_max_amps[0] */
+#define PSGD_HY_MAX_ELEM 5     /* grad_clip_max_amps[1] */
+#define PSGD_HY_MOM_BETA 6     /* momentum factor of this step */
+#define PSGD_HY_COUNT 8
+
+/* Gradient staging on 32 x 32 tiles of an n1 x n2 gradient G (fp32 or bf16, contiguous):
+ * x = G + (damping + eps |G|) * xi when xi != NULL (the damping noise of psgd_pro.py:122-123), else x = G.
+ *   PREP_NORMAL: out (n1 x n2, bf16 hi/lo)           = x
+ *   PREP_TRANS:  out (n2 x n1, bf16 hi/lo)           = (x * p2[j])^T
+ *   PREP_DIRECT: out_f32 (n1 x n2) = p1[i] x p2[j]   (both factors diagonal: the whole preconditioned gradient)
+ *               with optional part_row[tj][i], part_col[ti][j], part_tile[ti * tiles_j + tj] sums of squares.
+ * p1/p2 NULL mean ones. Replaces the exprP prologue of psgd_pro.py:123 and psgd_pro_fast.py:176. */
+#define PSGD_PREP_NORMAL 0
+#define PSGD_PREP_TRANS 1
+#define PSGD_PREP_DIRECT 2
+typedef struct PsgdPrepItem {
+  const void* g; int g_bf16; int mode;
+  const float* xi;
+  int n1, n2;
+  const float* p1; const float* p2;
+  void* out_hi; void* out_lo; long long ld_out;
+  float* out_f32;
+  float* part_row; float* part_col; float* part_tile;
+  float eps;
+} PsgdPrepItem;
+int psgd_prep(const PsgdPrepItem* items, const uint32_t* work, int nwork, const float* hyper, int* dev_err,
+              cudaStream_t stream);
+
+/* Start of the norm lower bound (psgd_pro.py:31-36 spd, :55-60 skh; psgd_pro_fast.py:32-38), one CTA per item:
+ * nf = max diag + tiny (spd) or max |A| + tiny (skh), j = argmax row norm (from part_row[row_slots][n]),
+ * V0 = A_j / nf + sgn(<A_j / nf, V_r>) V_r for the 32 rows of v, written as bf16 hi/lo (32 x n); *nf_out = nf. */
+typedef struct PsgdNlbPrepItem {
+  const void* a_hi; const void* a_lo; long long lda;
+  int n; int skew;
+  const float* part_row; int row_slots;
+  const float* diag;
+  const float* part_max; int max_slots;
+  const float* v;
+  void* v0_hi; void* v0_lo; long long ldv;
+  float* nf_out;
+} PsgdNlbPrepItem;
+int psgd_nlb_prep(const PsgdNlbPrepItem* items, int nitems, int* dev_err, cudaStream_t stream);
+
+/* Per-factor scalar work after the subspace iteration, one CTA per item (psgd_pro.py:126-135,
+ * psgd_pro_fast.py:178-189):
+ *   FACTOR_DENSE: ell = nf * max_c sqrt(sum_t part[t * ncols + c]) + term2  (the bound of the 4th product)
+ *   FACTOR_RANK1: ell = sum_t part[t] + term2                  (1-D gradient: term1 = Pg Pg^T, bound = |Pg|^2)
+ *   both: L = max(betaL L + (1 - betaL) ell, ell); *alpha = -lr/L; *beta = 1 + lr/L * term2
+ *         (the q update q - lr/L (term1 q - term2 q) as beta q + alpha term1 q)
+ *   FACTOR_DIAG: term1_i = sum_s part[s * n + i]; ell = max term1 + term2; L as above;
+ *         q_i *= 1 - lr/L (term1_i - term2); p_i = q_i^2.
+ *   FACTOR_SKEW: s = nf * max_c ||W4_c|| + tiny (the skew bound of R = Q - Q^T); tr(RQ) = sum(part_dot_rq) / s,
+ *         tr(RRQ) = -sum(part_dot_sq) / s^2; a = min(-tr(RQ)/tr(RRQ), 1/8) if tr(RRQ) < 0 else 1/8;
+ *         *alpha = a, *beta = 1 / s   (the Procrustes step of psgd_pro_fast.py:141-153). */
+#define PSGD_FACTOR_DENSE 0
+#define PSGD_FACTOR_RANK1 1
+#define PSGD_FACTOR_DIAG 2
+#define PSGD_FACTOR_SKEW 3
+typedef struct PsgdFactorItem {
+  int kind; int n; float term2;
+  float* L;
+  const float* nf; const float* part; int slots; int ncols;
+  float* alpha; float* beta;
+  float* q; float* p;
+  const float* part_dot_rq; int n_rq;
+  const float* part_dot_sq; int tiles_sq;
+} PsgdFactorItem;
+int psgd_factor_update(const PsgdFactorItem* items, int nitems, const float* hyper, int* dev_err,
+                       cudaStream_t stream);
+
+/* Rn = Q - Q^T on 32 x 32 tiles of an n x n fp32 Q (psgd_pro_fast.py:147; psgd_pro.py:87 up to sign), written
+ * as bf16 hi/lo, with part_row[tj][i] (row sums of squares), part_max[tile] (max |Rn|) and part_dot[tile]
+ * (sum Rn * Q) for tile = ti * tiles + tj. */
+typedef struct PsgdSkewItem {
+  const float* q; int n;
+  void* r_hi; void* r_lo; long long ldr;
+  float* part_row; float* part_max; float* part_dot;
+} PsgdSkewItem;
+int psgd_skew(const PsgdSkewItem* items, const uint32_t* work, int nwork, int* dev_err, cudaStream_t stream);
+
+/* M = a (Rn / s) + a^2 / 2 ((S / s) / s) on 32 x 32 tiles (bf16 hi/lo in, bf16 hi/lo out in place of Rn), with
+ * a = *alpha and 1/s = *beta from PSGD_FACTOR_SKEW: the Procrustes multiplier of psgd_pro_fast.py:153. */
+typedef struct PsgdRotItem {
+  int n;
+  void* r_hi; void* r_lo; long long ldr;
+  const void* s_hi; const void* s_lo; long long lds;
+  const float* alpha; const float* beta;
+} PsgdRotItem;
+int psgd_rot(const PsgdRotItem* items, const uint32_t* work, int nwork, int* dev_err, cudaStream_t stream);
+
+/* Clip and apply (psgd_pro.py:371-381, branch-free as psgd_pro_fast.py:426-438): per parameter
+ * avg = sqrt(sum(part) / numel), g = clamp(pg * min(1, max_avg / avg), +-max_elem), param -= lr_params * g.
+ * Work items are (item, chunk) pairs over chunks of PSGD_APPLY_CHUNK elements. */
+#define PSGD_APPLY_CHUNK 8192
+typedef struct PsgdApplyItem {
+  void* param; int param_bf16; long long numel;
+  const float* pg;
+  const float* part; int nparts;
+  float* scale;   /* scratch: the clip scale of this parameter (written by the first pass) */
+} PsgdApplyItem;
+int psgd_apply(const PsgdApplyItem* items, int nitems, const uint32_t* work, int nwork, const float* hyper,
+               int* dev_err, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -37,6 +37,44 @@ class GemmSpec(ctypes.Structure):
     ]
 
 
+class PrepItem(ctypes.Structure):
+    _fields_ = [("g", c_vp), ("g_bf16", c_int), ("mode", c_int), ("xi", c_vp), ("n1", c_int), ("n2", c_int),
+                ("p1", c_vp), ("p2", c_vp), ("out_hi", c_vp), ("out_lo", c_vp), ("ld_out", c_ll),
+                ("out_f32", c_vp), ("part_row", c_vp), ("part_col", c_vp), ("part_tile", c_vp), ("eps", c_float)]
+
+
+class NlbPrepItem(ctypes.Structure):
+    _fields_ = [("a_hi", c_vp), ("a_lo", c_vp), ("lda", c_ll), ("n", c_int), ("skew", c_int),
+                ("part_row", c_vp), ("row_slots", c_int), ("diag", c_vp), ("part_max", c_vp), ("max_slots", c_int),
+                ("v", c_vp), ("v0_hi", c_vp), ("v0_lo", c_vp), ("ldv", c_ll), ("nf_out", c_vp)]
+
+
+class FactorItem(ctypes.Structure):
+    _fields_ = [("kind", c_int), ("n", c_int), ("term2", c_float), ("L", c_vp), ("nf", c_vp), ("part", c_vp),
+                ("slots", c_int), ("ncols", c_int), ("alpha", c_vp), ("beta", c_vp), ("q", c_vp), ("p", c_vp),
+                ("part_dot_rq", c_vp), ("n_rq", c_int), ("part_dot_sq", c_vp), ("tiles_sq", c_int)]
+
+
+class SkewItem(ctypes.Structure):
+    _fields_ = [("q", c_vp), ("n", c_int), ("r_hi", c_vp), ("r_lo", c_vp), ("ldr", c_ll), ("part_row", c_vp),
+                ("part_max", c_vp), ("part_dot", c_vp)]
+
+
+class RotItem(ctypes.Structure):
+    _fields_ = [("n", c_int), ("r_hi", c_vp), ("r_lo", c_vp), ("ldr", c_ll), ("s_hi", c_vp), ("s_lo", c_vp),
+                ("lds", c_ll), ("alpha", c_vp), ("beta", c_vp)]
+
+
+class ApplyItem(ctypes.Structure):
+    _fields_ = [("param", c_vp), ("param_bf16", c_int), ("numel", c_ll), ("pg", c_vp), ("part", c_vp),
+                ("nparts", c_int), ("scale", c_vp)]
+
+
+PSGD_PREP_NORMAL, PSGD_PREP_TRANS, PSGD_PREP_DIRECT = 0, 1, 2
+PSGD_FACTOR_DENSE, PSGD_FACTOR_RANK1, PSGD_FACTOR_DIAG, PSGD_FACTOR_SKEW = 0, 1, 2, 3
+HY_LR_PRECOND, HY_BETA_L, HY_DAMPING, HY_LR_PARAMS, HY_MAX_AVG, HY_MAX_ELEM, HY_MOM_BETA, HY_COUNT = range(8)
+APPLY_CHUNK = 8192
+
 # (name, restype, argtypes) of every exported entry point; tests check that each symbol is present.
 SIGNATURES = [
     ("psgd_num_sms", c_int, []),
@@ -46,6 +84,12 @@ SIGNATURES = [
     ("psgd_gemm_encode", c_int, [ctypes.POINTER(GemmSpec), c_int, c_vp, ctypes.c_size_t, c_vp, c_int,
                                  ctypes.POINTER(c_int)]),
     ("psgd_gemm_launch", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp]),
+    ("psgd_prep", c_int, [c_vp, c_vp, c_int, c_vp, c_vp, c_vp]),
+    ("psgd_nlb_prep", c_int, [c_vp, c_int, c_vp, c_vp]),
+    ("psgd_factor_update", c_int, [c_vp, c_int, c_vp, c_vp, c_vp]),
+    ("psgd_skew", c_int, [c_vp, c_vp, c_int, c_vp, c_vp]),
+    ("psgd_rot", c_int, [c_vp, c_vp, c_int, c_vp, c_vp]),
+    ("psgd_apply", c_int, [c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_vp]),
 ]
 
 _lib = None

@@ -95,7 +95,11 @@ __device__ void epilogue_tile(const GemmDesc& d, int tm, int tn, uint32_t tacc, 
   const float alpha = s.alpha * (s.alpha_ptr ? __ldg(s.alpha_ptr) : 1.f);
   const float beta = s.beta * (s.beta_ptr ? __ldg(s.beta_ptr) : 1.f);
   const float rsc = (s.row_scale && rvalid) ? s.row_scale[gr] : 1.f;
+  // Column scales. For the subspace products (cs_mode) the value is (D * 1/(|W_c| + tiny)) * 1/nf: two separate
+  // multiplications in the reference's order (normalise V, then multiply by A / nf), so a zero matrix (nf = tiny)
+  // gives zeros instead of 0 * inf.
   const bool has_cs = s.col_scale != nullptr || s.cs_mode != 0;
+  const float inv_nf = s.cs_mode ? 1.f / *s.cs_nf : 1.f;
   if (has_cs) {
     for (int c = et; c < bn; c += 128) {
       const long long gc = n0 + c;
@@ -103,15 +107,10 @@ __device__ void epilogue_tile(const GemmDesc& d, int tm, int tn, uint32_t tacc, 
       if (gc < s.N) {
         if (s.col_scale) {
           v = s.col_scale[gc];
-        } else {
-          const float nf = *s.cs_nf;
-          if (s.cs_mode == 1) {
-            v = 1.f / nf;
-          } else {
-            float acc = 0.f;
-            for (int t = 0; t < s.cs_T; ++t) acc += s.cs_part[(long long)t * s.N + gc];
-            v = 1.f / (nf * (sqrtf(acc) + FLT_MIN));
-          }
+        } else if (s.cs_mode == 2) {
+          float acc = 0.f;
+          for (int t = 0; t < s.cs_T; ++t) acc += s.cs_part[(long long)t * s.N + gc];
+          v = 1.f / (sqrtf(acc) + FLT_MIN);
         }
       }
       cs[c] = v;
@@ -140,7 +139,7 @@ __device__ void epilogue_tile(const GemmDesc& d, int tm, int tn, uint32_t tacc, 
         float x = v[j] * alpha;
         if (s.aux) x += beta * s.aux[gr * s.ld_aux + gc0 + j];
         x *= rsc;
-        if (has_cs) x *= cs[c0 + j];
+        if (has_cs) x = (x * cs[c0 + j]) * inv_nf;
         v[j] = x;
       } else {
         v[j] = 0.f;
@@ -545,12 +544,27 @@ static int num_sms() {
   return n;
 }
 
+// Raises the dynamic shared-memory limit of a kernel once per device (never inside a graph capture afterwards).
+static bool smem_attr_once(const void* fn, int bytes) {
+  static const void* done[64][8] = {};  // per device: kernels already configured
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  for (int i = 0; i < 8; ++i)
+    if (done[dev][i] == fn) return true;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
+  for (int i = 0; i < 8; ++i)
+    if (done[dev][i] == nullptr) {
+      done[dev][i] = fn;
+      break;
+    }
+  return true;
+}
+
 template <int SPLIT, int BNMAX, int STAGES>
 static int launch_group(const GemmDesc* descs, const uint32_t* tiles, int ntiles, int* err, cudaStream_t st) {
   using C = GemmCfg<SPLIT, BNMAX, STAGES>;
   auto k = gemm_group_kernel<SPLIT, BNMAX, STAGES>;
-  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
-    return PSGD_ELAUNCH;
+  if (!smem_attr_once(reinterpret_cast<const void*>(k), C::SMEM_BYTES)) return PSGD_ELAUNCH;
   const int grid = ntiles < num_sms() ? ntiles : num_sms();
   k<<<grid, GEMM_THREADS, C::SMEM_BYTES, st>>>(descs, tiles, ntiles, err);
   return cudaGetLastError() == cudaSuccess ? PSGD_OK : PSGD_ELAUNCH;
@@ -560,8 +574,7 @@ template <int SPLIT, int BNMAX, int STAGES>
 static int launch_single(const GemmDesc& desc, const uint32_t* tiles, int ntiles, int* err, cudaStream_t st) {
   using C = GemmCfg<SPLIT, BNMAX, STAGES>;
   auto k = gemm_single_kernel<SPLIT, BNMAX, STAGES>;
-  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
-    return PSGD_ELAUNCH;
+  if (!smem_attr_once(reinterpret_cast<const void*>(k), C::SMEM_BYTES)) return PSGD_ELAUNCH;
   const int grid = ntiles < num_sms() ? ntiles : num_sms();
   k<<<grid, GEMM_THREADS, C::SMEM_BYTES, st>>>(desc, tiles, ntiles, err);
   return cudaGetLastError() == cudaSuccess ? PSGD_OK : PSGD_ELAUNCH;

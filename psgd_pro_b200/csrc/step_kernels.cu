@@ -1,0 +1,462 @@
+// Memory-bound kernels of the PSGD-Kron step (everything that is not a tensor-core contraction): gradient
+// staging with the damping noise, the start of the norm lower bounds, per-factor scalar updates (L, the diagonal
+// factors, the Procrustes step size), Rn = Q - Q^T, the Procrustes multiplier, and clip + apply.
+// Grouped: one launch covers every parameter / factor of a phase through a device item array (and a tile work
+// list for the tiled kernels). Reductions are deterministic (fixed-order partials, no atomics).
+#include "common.cuh"
+#include "psgd_b200.h"
+
+#include <float.h>
+
+namespace psgd {
+
+constexpr int TT = 32;        // tile edge of the tiled element-wise kernels
+constexpr int TROWS = 8;      // threads per tile column (256 threads, 4 rows each)
+
+PSGD_DEVI float load_g(const void* g, int bf16, long long idx) {
+  return bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(g)[idx])
+              : reinterpret_cast<const float*>(g)[idx];
+}
+
+PSGD_DEVI void store_split(void* hi, void* lo, long long idx, float v) {
+  __nv_bfloat16 h, l;
+  split_bf16(v, h, l);
+  reinterpret_cast<__nv_bfloat16*>(hi)[idx] = h;
+  if (lo) reinterpret_cast<__nv_bfloat16*>(lo)[idx] = l;
+}
+
+PSGD_DEVI float load_split(const void* hi, const void* lo, long long idx) {
+  float v = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(hi)[idx]);
+  if (lo) v += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(lo)[idx]);
+  return v;
+}
+
+// ---- gradient staging ------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) prep_kernel(const PsgdPrepItem* __restrict__ items,
+                                                  const uint32_t* __restrict__ work, int nwork,
+                                                  const float* __restrict__ hyper) {
+  __shared__ float tile[TT][TT + 1];
+  __shared__ float colred[TROWS][TT];
+  __shared__ float tred[TROWS];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const float damping = hyper[PSGD_HY_DAMPING];
+  for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
+    const PsgdPrepItem& it = items[work[2 * w]];
+    const int ti = work[2 * w + 1] >> 16, tj = work[2 * w + 1] & 0xFFFF;
+    const int i0 = ti * TT, j0 = tj * TT;
+    const int j = j0 + tx;
+    float vals[TT / TROWS];
+#pragma unroll
+    for (int u = 0; u < TT / TROWS; ++u) {
+      const int i = i0 + ty + u * TROWS;
+      float x = 0.f;
+      if (i < it.n1 && j < it.n2) {
+        const long long idx = (long long)i * it.n2 + j;
+        x = load_g(it.g, it.g_bf16, idx);
+        if (it.xi) x += (damping + it.eps * fabsf(x)) * it.xi[idx];
+      }
+      vals[u] = x;
+    }
+    if (it.mode == PSGD_PREP_NORMAL) {
+#pragma unroll
+      for (int u = 0; u < TT / TROWS; ++u) {
+        const int i = i0 + ty + u * TROWS;
+        if (i < it.n1 && j < it.n2) store_split(it.out_hi, it.out_lo, (long long)i * it.ld_out + j, vals[u]);
+      }
+    } else if (it.mode == PSGD_PREP_TRANS) {
+      const float s2 = (it.p2 && j < it.n2) ? it.p2[j] : 1.f;
+#pragma unroll
+      for (int u = 0; u < TT / TROWS; ++u) tile[ty + u * TROWS][tx] = vals[u] * s2;
+      __syncthreads();
+#pragma unroll
+      for (int u = 0; u < TT / TROWS; ++u) {
+        const int jj = j0 + ty + u * TROWS, ii = i0 + tx;  // output row jj, column ii
+        if (jj < it.n2 && ii < it.n1) store_split(it.out_hi, it.out_lo, (long long)jj * it.ld_out + ii, tile[tx][ty + u * TROWS]);
+      }
+      __syncthreads();
+    } else {  // PSGD_PREP_DIRECT
+      const float s2 = (it.p2 && j < it.n2) ? it.p2[j] : 1.f;
+      float csum = 0.f, tsum = 0.f;
+#pragma unroll
+      for (int u = 0; u < TT / TROWS; ++u) {
+        const int i = i0 + ty + u * TROWS;
+        const bool ok = i < it.n1 && j < it.n2;
+        const float s1 = (it.p1 && i < it.n1) ? it.p1[i] : 1.f;
+        const float v = ok ? s1 * vals[u] * s2 : 0.f;
+        if (ok && it.out_f32) it.out_f32[(long long)i * it.n2 + j] = v;
+        const float v2 = v * v;
+        csum += v2;
+        const float rs = warp_sum(v2);  // this warp holds one row of the tile
+        if (tx == 0 && it.part_row && i < it.n1) it.part_row[(long long)tj * it.n1 + i] = rs;
+        tsum += rs;
+      }
+      colred[ty][tx] = csum;
+      if (tx == 0) tred[ty] = tsum;
+      __syncthreads();
+      if (ty == 0) {
+        float c = 0.f;
+#pragma unroll
+        for (int r = 0; r < TROWS; ++r) c += colred[r][tx];
+        if (it.part_col && j < it.n2) it.part_col[(long long)ti * it.n2 + j] = c;
+        if (tx == 0 && it.part_tile) {
+          float t = 0.f;
+#pragma unroll
+          for (int r = 0; r < TROWS; ++r) t += tred[r];
+          const int tiles_j = (it.n2 + TT - 1) / TT;
+          it.part_tile[(long long)ti * tiles_j + tj] = t;
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// ---- norm lower bound start --------------------------------------------------------------------------------------
+constexpr int NLB_THREADS = 512;
+
+__global__ void __launch_bounds__(NLB_THREADS) nlb_prep_kernel(const PsgdNlbPrepItem* __restrict__ items) {
+  const PsgdNlbPrepItem& it = items[blockIdx.x];
+  const int n = it.n, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  __shared__ float s_val[NLB_THREADS / 32];
+  __shared__ int s_idx[NLB_THREADS / 32];
+  __shared__ float s_dot[32][NLB_THREADS / 32];
+  __shared__ float s_nf;
+  __shared__ int s_j;
+  // argmax of row norms (first maximum) and the normalising factor
+  float best = -1.f, mx = 0.f;
+  int bj = 0x7fffffff;
+  for (int i = tid; i < n; i += NLB_THREADS) {
+    float r = 0.f;
+    for (int s = 0; s < it.row_slots; ++s) r += it.part_row[(long long)s * n + i];
+    if (r > best) { best = r; bj = i; }
+    if (!it.skew) mx = fmaxf(mx, it.diag[i]);
+  }
+  if (it.skew)
+    for (int t = tid; t < it.max_slots; t += NLB_THREADS) mx = fmaxf(mx, it.part_max[t]);
+  if (!it.skew && tid >= n) mx = -FLT_MAX;
+  // reduce (value desc, index asc) and max
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oj = __shfl_xor_sync(0xffffffffu, bj, o);
+    if (ob > best || (ob == best && oj < bj)) { best = ob; bj = oj; }
+  }
+  const float wmx = warp_max(mx);
+  if (lane == 0) { s_val[wid] = best; s_idx[wid] = bj; s_dot[0][wid] = wmx; }
+  __syncthreads();
+  if (tid == 0) {
+    float b = s_val[0], m = s_dot[0][0];
+    int jj = s_idx[0];
+    for (int w = 1; w < NLB_THREADS / 32; ++w) {
+      if (s_val[w] > b || (s_val[w] == b && s_idx[w] < jj)) { b = s_val[w]; jj = s_idx[w]; }
+      m = fmaxf(m, s_dot[0][w]);
+    }
+    s_nf = m + FLT_MIN;  // + smallest normal (psgd_pro.py:32, :56)
+    s_j = (jj >= n || jj < 0) ? 0 : jj;
+    *it.nf_out = s_nf;
+  }
+  __syncthreads();
+  const float nf = s_nf;
+  const long long rowj = (long long)s_j * it.lda;
+  // dots <A_j / nf, V_r> for the 32 rows
+  float dot[32];
+#pragma unroll
+  for (int r = 0; r < 32; ++r) dot[r] = 0.f;
+  for (int k = tid; k < n; k += NLB_THREADS) {
+    const float a = load_split(it.a_hi, it.a_lo, rowj + k) / nf;
+#pragma unroll
+    for (int r = 0; r < 32; ++r) dot[r] += a * it.v[(long long)r * n + k];
+  }
+#pragma unroll
+  for (int r = 0; r < 32; ++r) {
+    const float d = warp_sum(dot[r]);
+    if (lane == 0) s_dot[r][wid] = d;
+  }
+  __syncthreads();
+  if (tid < 32) {
+    float d = 0.f;
+    for (int w = 0; w < NLB_THREADS / 32; ++w) d += s_dot[tid][w];
+    s_dot[tid][0] = d > 0.f ? 1.f : (d < 0.f ? -1.f : 0.f);  // torch.sgn
+  }
+  __syncthreads();
+  for (int k = tid; k < n; k += NLB_THREADS) {
+    const float a = load_split(it.a_hi, it.a_lo, rowj + k) / nf;
+#pragma unroll
+    for (int r = 0; r < 32; ++r)
+      store_split(it.v0_hi, it.v0_lo, (long long)r * it.ldv + k, a + s_dot[r][0] * it.v[(long long)r * n + k]);
+  }
+}
+
+// ---- per-factor scalars ------------------------------------------------------------------------------------------
+constexpr int FAC_THREADS = 256;
+
+PSGD_DEVI float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+  return t;
+}
+
+PSGD_DEVI float block_max(float v, float* red) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  float t = -FLT_MAX;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t = fmaxf(t, red[w]);
+  return t;
+}
+
+// max over columns c < ncols of sqrt(sum_t part[t * ncols + c])
+PSGD_DEVI float max_col_norm(const float* part, int slots, int ncols, float* red) {
+  float m = 0.f;
+  for (int c = threadIdx.x; c < ncols; c += blockDim.x) {
+    float s = 0.f;
+    for (int t = 0; t < slots; ++t) s += part[(long long)t * ncols + c];
+    m = fmaxf(m, sqrtf(s));
+  }
+  return block_max(m, red);
+}
+
+__global__ void __launch_bounds__(FAC_THREADS) factor_kernel(const PsgdFactorItem* __restrict__ items,
+                                                            const float* __restrict__ hyper) {
+  const PsgdFactorItem& it = items[blockIdx.x];
+  __shared__ float red[FAC_THREADS / 32];
+  const float lr = hyper[PSGD_HY_LR_PRECOND], betaL = hyper[PSGD_HY_BETA_L];
+  if (it.kind == PSGD_FACTOR_DENSE || it.kind == PSGD_FACTOR_RANK1) {
+    float ell;
+    if (it.kind == PSGD_FACTOR_DENSE) {
+      ell = *it.nf * max_col_norm(it.part, it.slots, it.ncols, red) + it.term2;
+    } else {
+      float s = 0.f;
+      for (int t = threadIdx.x; t < it.slots; t += blockDim.x) s += it.part[t];
+      ell = block_sum(s, red) + it.term2;
+    }
+    if (threadIdx.x == 0) {
+      const float Lold = *it.L;
+      const float L = fmaxf(betaL * Lold + (1.f - betaL) * ell, ell);
+      *it.L = L;
+      const float coef = lr / L;
+      *it.alpha = -coef;
+      *it.beta = 1.f + coef * it.term2;
+    }
+  } else if (it.kind == PSGD_FACTOR_DIAG) {
+    const int n = it.n;
+    float m = -FLT_MAX;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      float t1 = 0.f;
+      for (int s = 0; s < it.slots; ++s) t1 += it.part[(long long)s * n + i];
+      m = fmaxf(m, t1);
+    }
+    const float ell = block_max(m, red) + it.term2;
+    const float Lold = *it.L;
+    const float L = fmaxf(betaL * Lold + (1.f - betaL) * ell, ell);
+    const float coef = lr / L;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      float t1 = 0.f;
+      for (int s = 0; s < it.slots; ++s) t1 += it.part[(long long)s * n + i];
+      const float q = it.q[i] * (1.f - coef * (t1 - it.term2));
+      it.q[i] = q;
+      it.p[i] = q * q;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *it.L = L;
+  } else {  // PSGD_FACTOR_SKEW
+    const float s = *it.nf * max_col_norm(it.part, it.slots, it.ncols, red) + FLT_MIN;
+    float a1 = 0.f;
+    for (int t = threadIdx.x; t < it.n_rq; t += blockDim.x) a1 += it.part_dot_rq[t];
+    const float sum_rq = block_sum(a1, red);
+    float a2 = 0.f;
+    const int T = it.tiles_sq;
+    for (int t = threadIdx.x; t < T * T; t += blockDim.x) {
+      const int tm = t / T, tn = t % T;
+      if (tm <= tn) a2 += it.part_dot_sq[t];
+    }
+    const float sum_sq = block_sum(a2, red);
+    if (threadIdx.x == 0) {
+      // divide step by step, as the reference normalises R before its products: with R = 0 (Q exactly
+      // symmetric) s is the smallest normal and every quotient stays finite
+      const float tr_rq = sum_rq / s;
+      const float tr_rrq = -((sum_sq / s) / s);
+      const float amax = 0.125f;
+      const float a = tr_rrq < 0.f ? fminf(-tr_rq / tr_rrq, amax) : amax;
+      *it.alpha = a;
+      *it.beta = 1.f / s;
+    }
+  }
+}
+
+// ---- Rn = Q - Q^T ------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) skew_kernel(const PsgdSkewItem* __restrict__ items,
+                                                  const uint32_t* __restrict__ work, int nwork) {
+  __shared__ float tT[TT][TT + 1];
+  __shared__ float colred[TROWS][2];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
+    const PsgdSkewItem& it = items[work[2 * w]];
+    const int ti = work[2 * w + 1] >> 16, tj = work[2 * w + 1] & 0xFFFF;
+    const int n = it.n, i0 = ti * TT, j0 = tj * TT;
+    // Q^T tile: tT[c][r] = Q[j0 + c][i0 + r] loaded coalesced along r
+#pragma unroll
+    for (int u = 0; u < TT / TROWS; ++u) {
+      const int c = ty + u * TROWS, gi = j0 + c, gj = i0 + tx;
+      tT[c][tx] = (gi < n && gj < n) ? it.q[(long long)gi * n + gj] : 0.f;
+    }
+    __syncthreads();
+    float mx = 0.f, dsum = 0.f;
+    const int j = j0 + tx;
+#pragma unroll
+    for (int u = 0; u < TT / TROWS; ++u) {
+      const int r = ty + u * TROWS, i = i0 + r;
+      float v = 0.f, q = 0.f;
+      if (i < n && j < n) {
+        q = it.q[(long long)i * n + j];
+        v = q - tT[tx][r];  // Q[i][j] - Q[j][i]
+        store_split(it.r_hi, it.r_lo, (long long)i * it.ldr + j, v);
+      }
+      const float rs = warp_sum(v * v);
+      if (tx == 0 && i < n) it.part_row[(long long)tj * n + i] = rs;
+      mx = fmaxf(mx, fabsf(v));
+      dsum += v * q;
+    }
+    mx = warp_max(mx);
+    dsum = warp_sum(dsum);
+    if (tx == 0) { colred[ty][0] = mx; colred[ty][1] = dsum; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float m = 0.f, d = 0.f;
+      for (int r = 0; r < TROWS; ++r) { m = fmaxf(m, colred[r][0]); d += colred[r][1]; }
+      const int tiles = (n + TT - 1) / TT;
+      it.part_max[(long long)ti * tiles + tj] = m;
+      it.part_dot[(long long)ti * tiles + tj] = d;
+    }
+    __syncthreads();
+  }
+}
+
+// ---- M = alpha Rn + beta S ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) rot_kernel(const PsgdRotItem* __restrict__ items,
+                                                 const uint32_t* __restrict__ work, int nwork) {
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
+    const PsgdRotItem& it = items[work[2 * w]];
+    const int ti = work[2 * w + 1] >> 16, tj = work[2 * w + 1] & 0xFFFF;
+    const float a = *it.alpha, inv_s = *it.beta, half_a2 = 0.5f * a * a;
+    const int j = tj * TT + tx;
+#pragma unroll
+    for (int u = 0; u < TT / TROWS; ++u) {
+      const int i = ti * TT + ty + u * TROWS;
+      if (i < it.n && j < it.n) {
+        const float r = load_split(it.r_hi, it.r_lo, (long long)i * it.ldr + j);
+        const float s = load_split(it.s_hi, it.s_lo, (long long)i * it.lds + j);
+        // M = a Rn/s + a^2/2 (S/s)/s, with the normalised factors formed first (no overflow for tiny s)
+        store_split(it.r_hi, it.r_lo, (long long)i * it.ldr + j, a * (r * inv_s) + half_a2 * ((s * inv_s) * inv_s));
+      }
+    }
+  }
+}
+
+// ---- clip + apply ------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) clip_scale_kernel(const PsgdApplyItem* __restrict__ items,
+                                                        const float* __restrict__ hyper) {
+  const PsgdApplyItem& it = items[blockIdx.x];
+  __shared__ float red[8];
+  float s = 0.f;
+  for (int t = threadIdx.x; t < it.nparts; t += blockDim.x) s += it.part[t];
+  const float tot = block_sum(s, red);
+  if (threadIdx.x == 0) {
+    const float avg = sqrtf(tot / (float)it.numel);
+    // clamp(max_avg / avg, max = 1): exactly 1 when the reference's branch would not fire
+    *it.scale = fminf(hyper[PSGD_HY_MAX_AVG] / avg, 1.f);
+  }
+}
+
+__global__ void __launch_bounds__(256) apply_kernel(const PsgdApplyItem* __restrict__ items,
+                                                   const uint32_t* __restrict__ work, int nwork,
+                                                   const float* __restrict__ hyper) {
+  const float lr = hyper[PSGD_HY_LR_PARAMS], me = hyper[PSGD_HY_MAX_ELEM];
+  for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
+    const PsgdApplyItem& it = items[work[2 * w]];
+    const long long base = (long long)work[2 * w + 1] * PSGD_APPLY_CHUNK;
+    const float sc = *it.scale;
+    const long long end = min(base + (long long)PSGD_APPLY_CHUNK, it.numel);
+    for (long long k = base + threadIdx.x; k < end; k += blockDim.x) {
+      const float g = fminf(fmaxf(it.pg[k] * sc, -me), me);
+      if (it.param_bf16) {
+        __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(it.param);
+        p[k] = __float2bfloat16_rn(__bfloat162float(p[k]) - lr * g);
+      } else {
+        float* p = reinterpret_cast<float*>(it.param);
+        p[k] = p[k] - lr * g;
+      }
+    }
+  }
+}
+
+static int grid_for(int nwork) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int cap = sms * 8;
+  return nwork < cap ? nwork : cap;
+}
+
+static int launched() { return cudaGetLastError() == cudaSuccess ? PSGD_OK : PSGD_ELAUNCH; }
+
+}  // namespace psgd
+
+using namespace psgd;
+
+extern "C" int psgd_prep(const PsgdPrepItem* items, const uint32_t* work, int nwork, const float* hyper, int* dev_err,
+                         cudaStream_t stream) {
+  if (!items || !work || !hyper || nwork < 0) return PSGD_EINVAL;
+  if (nwork == 0) return PSGD_OK;
+  prep_kernel<<<grid_for(nwork), 256, 0, stream>>>(items, work, nwork, hyper);
+  return launched();
+}
+
+extern "C" int psgd_nlb_prep(const PsgdNlbPrepItem* items, int nitems, int* dev_err, cudaStream_t stream) {
+  if (!items || nitems < 0) return PSGD_EINVAL;
+  if (nitems == 0) return PSGD_OK;
+  nlb_prep_kernel<<<nitems, NLB_THREADS, 0, stream>>>(items);
+  return launched();
+}
+
+extern "C" int psgd_factor_update(const PsgdFactorItem* items, int nitems, const float* hyper, int* dev_err,
+                                  cudaStream_t stream) {
+  if (!items || !hyper || nitems < 0) return PSGD_EINVAL;
+  if (nitems == 0) return PSGD_OK;
+  factor_kernel<<<nitems, FAC_THREADS, 0, stream>>>(items, hyper);
+  return launched();
+}
+
+extern "C" int psgd_skew(const PsgdSkewItem* items, const uint32_t* work, int nwork, int* dev_err,
+                         cudaStream_t stream) {
+  if (!items || !work || nwork < 0) return PSGD_EINVAL;
+  if (nwork == 0) return PSGD_OK;
+  skew_kernel<<<grid_for(nwork), 256, 0, stream>>>(items, work, nwork);
+  return launched();
+}
+
+extern "C" int psgd_rot(const PsgdRotItem* items, const uint32_t* work, int nwork, int* dev_err,
+                        cudaStream_t stream) {
+  if (!items || !work || nwork < 0) return PSGD_EINVAL;
+  if (nwork == 0) return PSGD_OK;
+  rot_kernel<<<grid_for(nwork), 256, 0, stream>>>(items, work, nwork);
+  return launched();
+}
+
+extern "C" int psgd_apply(const PsgdApplyItem* items, int nitems, const uint32_t* work, int nwork,
+                          const float* hyper, int* dev_err, cudaStream_t stream) {
+  if (!items || !work || !hyper || nitems < 0 || nwork < 0) return PSGD_EINVAL;
+  if (nitems == 0) return PSGD_OK;
+  clip_scale_kernel<<<nitems, 256, 0, stream>>>(items, hyper);
+  int rc = launched();
+  if (rc) return rc;
+  if (nwork == 0) return PSGD_OK;
+  apply_kernel<<<grid_for(nwork), 256, 0, stream>>>(items, work, nwork, hyper);
+  return launched();
+}

@@ -1,0 +1,71 @@
+"""Shared helpers for the parity tests: golden fixture loading and the reference-order random draw stream
+(the same stream tests/golden/make_golden.py served to the reference)."""
+import json
+import os
+
+import numpy as np
+
+from oracle import psgd_oracle as O
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+SCEN = ["config1", "mixed_inf", "mixed_skew1", "whiten_momentum", "prob_half"]
+
+
+def rel(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    nb = np.linalg.norm(b)
+    return float(np.linalg.norm(a - b) / nb) if nb > 0 else float(np.linalg.norm(a - b))
+
+
+def load(name):
+    z = np.load(os.path.join(GOLD, name + ".npz"))
+    return {k: z[k] for k in z.files}
+
+
+def meta_of(g):
+    meta = json.loads(str(g["meta"]))
+    meta["kw"] = {k: (float("inf") if v == "inf" else v) for k, v in meta["kw"].items()}
+    return meta
+
+
+def reference_order_draws(rng, QL, shapes, prob, forced):
+    """One step's draws in the order psgd_pro.KronWhiten.step asks for them: the update coin (psgd_pro.py:345),
+    then per parameter randn_like(G) (:123), randn(32, n) for each dense factor's two norm bounds (:35, :59) and
+    the balancing coin (:138). QL: the oracle's per-parameter (Q list, L list), which fixes dense/diagonal."""
+    u = float(rng.random(dtype=np.float32))
+    d = {"update": u, "coins": [], "normals": []}
+    if not u < prob:
+        return d
+    for k, (ql, shp) in enumerate(zip(QL, shapes)):
+        nd = [np.asarray(rng.standard_normal(shp, dtype=np.float32))]
+        for q in ql[0]:
+            if q.ndim == 2:
+                nd += [rng.standard_normal((O.K_SUBSPACE, q.shape[0]), dtype=np.float32) for _ in range(2)]
+        c = float(rng.random(dtype=np.float32))
+        d["normals"].append(nd)
+        d["coins"].append(0.0 if k in forced else c)
+    return d
+
+
+class Scenario:
+    """Parameters, per-step gradients and draws of a golden scenario, in the reference order."""
+
+    def __init__(self, name):
+        self.g = load(name)
+        self.meta = meta_of(self.g)
+        m = self.meta
+        self.rng_params = np.random.default_rng(1000 + m["seed"])
+        self.rng_grads = np.random.default_rng(2000 + m["seed"])
+        self.rng_draws = np.random.default_rng(3000 + m["seed"])
+        self.params = [np.asarray(self.rng_params.standard_normal(tuple(s), dtype=np.float32)) for s in m["shapes"]]
+
+    def grads(self):
+        m = self.meta
+        return [np.asarray(self.rng_grads.standard_normal(tuple(s), dtype=np.float32) * np.float32(sc),
+                           dtype=np.float32) for s, sc in zip(m["shapes"], m["grad_scale"])]
+
+    def draws(self, step, QL, grads):
+        shapes = [np.squeeze(x).shape for x in grads]
+        forced = self.meta["force_balance"].get(str(step), [])
+        prob = self.meta["kw"].get("preconditioner_update_probability", 1.0)
+        return reference_order_draws(self.rng_draws, QL, shapes, prob, forced)

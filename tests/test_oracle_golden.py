@@ -1,69 +1,23 @@
 """Pins the CPU oracle (oracle/psgd_oracle.py) to the reference: the golden vectors in tests/golden/ were made by
 running the reference itself (tests/golden/make_golden.py) on seeded inputs; here the oracle replays the same
 parameters, gradients and random draws and must land on the same Q, L, parameters and preconditioned gradients."""
-import json
-import os
-
 import numpy as np
 import pytest
 
 from oracle import psgd_oracle as O
-
-GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
-SCEN = ["config1", "mixed_inf", "mixed_skew1", "whiten_momentum", "prob_half"]
-
-
-def rel(a, b):
-    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
-    nb = np.linalg.norm(b)
-    return float(np.linalg.norm(a - b) / nb) if nb > 0 else float(np.linalg.norm(a - b))
-
-
-def load(name):
-    z = np.load(os.path.join(GOLD, name + ".npz"))
-    return {k: z[k] for k in z.files}
-
-
-def reference_order_draws(rng, opt, srcs, forced):
-    """One step's draws in the order psgd_pro.KronWhiten.step asks for them: the update coin (psgd_pro.py:345),
-    then per parameter randn_like(G) (:123), randn(32, n) for each dense factor's two norm bounds (:35, :59) and
-    the balancing coin (:138)."""
-    u = float(rng.random(dtype=np.float32))
-    d = {"update": u, "coins": [], "normals": []}
-    if not u < opt.preconditioner_update_probability:
-        return d
-    for k, (QL, g) in enumerate(zip(opt.QL, srcs)):
-        nd = [np.asarray(rng.standard_normal(g.shape, dtype=np.float32))]
-        for q in QL[0]:
-            if q.ndim == 2:
-                nd += [rng.standard_normal((O.K_SUBSPACE, q.shape[0]), dtype=np.float32) for _ in range(2)]
-        c = float(rng.random(dtype=np.float32))
-        d["normals"].append(nd)
-        d["coins"].append(0.0 if k in forced else c)
-    return d
+from scenario_util import SCEN, Scenario, load, rel
 
 
 def replay(name, dtype=np.float64):
-    g = load(name)
-    meta = json.loads(str(g["meta"]))
-    kw = {k: (float("inf") if v == "inf" else v) for k, v in meta["kw"].items()}
-    rng_params = np.random.default_rng(1000 + meta["seed"])
-    rng_grads = np.random.default_rng(2000 + meta["seed"])
-    rng_draws = np.random.default_rng(3000 + meta["seed"])
-    params = [np.asarray(rng_params.standard_normal(tuple(s), dtype=np.float32)) for s in meta["shapes"]]
-    opt = O.KronWhitenOracle(params, dtype=dtype, **kw)
+    sc = Scenario(name)
+    opt = O.KronWhitenOracle(sc.params, dtype=dtype, **sc.meta["kw"])
     pre = None
-    for step in range(1, meta["steps"] + 1):
-        G = [np.asarray(rng_grads.standard_normal(tuple(s), dtype=np.float32) * np.float32(sc), dtype=np.float32)
-             for s, sc in zip(meta["shapes"], meta["grad_scale"])]
-        Gs = [np.squeeze(x).astype(dtype) for x in G]
+    for step in range(1, sc.meta["steps"] + 1):
+        G = sc.grads()
         if opt.QL is None:
-            opt._init_on_the_fly(Gs)
-        # the update source (gradient or momentum) decides the noise shapes; both have the gradient's shape
-        forced = meta["force_balance"].get(str(step), [])
-        draws = reference_order_draws(rng_draws, opt, Gs, forced)
-        pre = opt.step(G, draws)
-    return g, opt, pre
+            opt._init_on_the_fly([np.squeeze(x).astype(dtype) for x in G])
+        pre = opt.step(G, sc.draws(step, opt.QL, G))
+    return sc.g, opt, pre
 
 
 @pytest.mark.parametrize("name", SCEN)

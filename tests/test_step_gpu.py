@@ -1,0 +1,113 @@
+"""End-to-end parity of psgd_pro_b200.KronWhiten (the sm_100a step) with the CPU oracle and the reference's golden
+outputs, on the golden scenarios with identical parameters, gradients and random draws.
+
+Tolerances (relative Frobenius error after the scenario's steps): precision="fp32" 1e-3 on every Q factor and the
+preconditioned gradient; precision="bf16" (one bf16 MMA per product, fp32 accumulation) 2e-2."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import psgd_oracle as O
+from psgd_pro_b200 import KronWhiten
+from scenario_util import SCEN, Scenario, rel
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"fp32": 1e-3, "bf16": 2e-2}
+
+
+def run_pair(name, precision, cuda):
+    sc = Scenario(name)
+    kw = sc.meta["kw"]
+    ora = O.KronWhitenOracle(sc.params, dtype=np.float64, **kw)
+    params = [torch.nn.Parameter(torch.from_numpy(p.copy()).to(cuda)) for p in sc.params]
+    opt = KronWhiten(params, precision=precision, **kw)
+    pre = None
+    for step in range(1, sc.meta["steps"] + 1):
+        G = sc.grads()
+        if ora.QL is None:
+            ora._init_on_the_fly([np.squeeze(x).astype(np.float64) for x in G])
+        draws = sc.draws(step, ora.QL, G)
+        pre = ora.step(G, draws)
+        opt.step_math([torch.from_numpy(x).to(cuda) for x in G], draws=draws)
+    torch.cuda.synchronize()
+    opt.check_errors()
+    return sc, ora, opt, pre
+
+
+@pytest.mark.parametrize("name", SCEN)
+@pytest.mark.parametrize("precision", ["fp32", "bf16"])
+def test_step_matches_oracle_and_reference(cuda, name, precision):
+    sc, ora, opt, pre = run_pair(name, precision, cuda)
+    tol = TOL[precision]
+    st = opt.state_dict()["state"]
+    for k, ((Qo, Lo), s) in enumerate(zip(ora.QL, st)):
+        for i, (qo, qg) in enumerate(zip(Qo, s["Q"])):
+            qg = qg.detach().cpu().numpy()
+            assert np.isfinite(qg).all()
+            e_ora = rel(qg, qo)
+            e_ref = rel(qg, sc.g[f"Q_{k}_{i}"])
+            assert e_ora < tol and e_ref < tol, (name, k, i, e_ora, e_ref)
+            lg = float(s["L"][i])
+            assert abs(lg - Lo[i]) <= tol * abs(Lo[i]) + 1e-30, (name, k, i, lg, Lo[i])
+        pg = opt._plan.params[k].pg32.detach().cpu().numpy().reshape(np.shape(pre[k]))
+        assert rel(pg, pre[k]) < tol, (name, k, rel(pg, pre[k]))
+        assert rel(pg, sc.g[f"pre_{k}"]) < tol
+        assert rel(opt._params_with_grad[k].detach().cpu().numpy(), sc.g[f"param_{k}"]) < tol
+
+
+def test_graphs_match_eager(cuda):
+    """Device-drawn noise: the captured CUDA-graph step gives bitwise the eager result from the same seed."""
+    torch.manual_seed(0)
+    shapes = [(96, 200), (300,), (64, 64), (5000, 48)]
+    base = [torch.randn(s) * 0.1 for s in shapes]
+    grads = [[torch.randn(s).to(cuda) * 1e-2 for s in shapes] for _ in range(4)]
+    out = []
+    for graphs in (False, True):
+        params = [torch.nn.Parameter(b.clone().to(cuda)) for b in base]
+        opt = KronWhiten(params, preconditioner_init_scale=1.0, preconditioner_max_skew=float("inf"),
+                         preconditioner_max_size=4096, cuda_graphs=graphs)
+        torch.manual_seed(123)
+        torch.cuda.manual_seed(123)
+        for g in grads:
+            opt.step_math(g)
+        torch.cuda.synchronize()
+        opt.check_errors()
+        out.append([p.detach().clone() for p in params] + [q for s in opt.state_dict()["state"] for q in s["Q"]])
+    for a, b in zip(*out):
+        assert torch.equal(a, b)
+
+
+def test_state_dict_roundtrip(cuda):
+    """Save after 2 steps, load into a fresh optimizer, continue: same result as an uninterrupted run."""
+    sc = Scenario("mixed_inf")
+    kw = dict(sc.meta["kw"], preconditioner_init_scale=0.8)
+    ora = O.KronWhitenOracle(sc.params, dtype=np.float64, **kw)
+    G_all = [sc.grads() for _ in range(4)]
+    D_all = []
+    for step, G in enumerate(G_all, 1):
+        d = sc.draws(step, ora.QL, G)
+        D_all.append(d)
+        ora.step(G, d)
+    mk = lambda: [torch.nn.Parameter(torch.from_numpy(p.copy()).to(cuda)) for p in sc.params]
+    pa = mk()
+    a = KronWhiten(pa, **kw)
+    for G, d in zip(G_all, D_all):
+        a.step_math([torch.from_numpy(x).to(cuda) for x in G], draws=d)
+    pb = mk()
+    b = KronWhiten(pb, **kw)
+    for G, d in zip(G_all[:2], D_all[:2]):
+        b.step_math([torch.from_numpy(x).to(cuda) for x in G], draws=d)
+    saved = {"state": [{"Q": [q.clone() for q in s["Q"]], "L": [l.clone() for l in s["L"]], "m": s["m"]}
+                       for s in b.state_dict()["state"]], "counter_m": 0}
+    pc = [torch.nn.Parameter(p.detach().clone()) for p in pb]
+    c = KronWhiten(pc, **kw)
+    c.load_state_dict(saved)
+    for G, d in zip(G_all[2:], D_all[2:]):
+        c.step_math([torch.from_numpy(x).to(cuda) for x in G], draws=d)
+    torch.cuda.synchronize()
+    for x, y in zip(a.state_dict()["state"], c.state_dict()["state"]):
+        for qa, qc in zip(x["Q"], y["Q"]):
+            assert rel(qc.cpu().numpy(), qa.cpu().numpy()) < 1e-5
+    for x, y in zip(pa, pc):
+        assert rel(y.detach().cpu().numpy(), x.detach().cpu().numpy()) < 1e-6
