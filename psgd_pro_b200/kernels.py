@@ -91,6 +91,7 @@ class GemmGroup:
         check(L.psgd_gemm_encode(self.specs, len(specs), host_table.data_ptr(), nbytes, host_tiles.data_ptr(),
                                  ntiles_max, ctypes.byref(nt)), "psgd_gemm_encode")
         self.ntiles = nt.value
+        self.flops = sum((s.M * s.M * s.K) if s.mode == PSGD_GEMM_SYRK else (2 * s.M * s.N * s.K) for s in specs)
         self.table = host_table.to(device)
         self.tiles = host_tiles[:2 * max(self.ntiles, 1)].to(device)
         assert self.table.data_ptr() % 64 == 0

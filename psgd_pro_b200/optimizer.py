@@ -498,21 +498,38 @@ class _Plan:
         self._launch(self.g_u22)
         tr("gram")
 
-    def run_apply(self):
+    def run_apply(self, trace=None):
         L, st, err, hy = _capi.lib(), K.stream_handle(), self.err.data_ptr(), self.hyper.data_ptr()
+        tr = trace or (lambda name: None)
         check(L.psgd_prep(self.prep_a_dev.data_ptr(), self.prep_a_work.data_ptr(), self.prep_a_n, hy, err, st), "prep")
+        tr("a_prep")
         self._launch(self.g_a1)
+        tr("a1")
         self._launch(self.g_a2)
+        tr("a2")
         check(L.psgd_apply(self.apply_dev.data_ptr(), self.apply_n, self.apply_work.data_ptr(), self.apply_nw, hy,
                            err, st), "apply")
+        tr("apply")
+
+    def phase_groups(self):
+        """(name, GemmGroup) of every tensor-core phase, in the names run_update / run_apply trace."""
+        out = [("u1", self.g_u1), ("u2", self.g_u2), ("term1", self.g_u3)]
+        out += [(f"nlb_spd{k}", g) for k, g in enumerate(self.g_spd)]
+        out += [("qupdate", self.g_u10)]
+        out += [(f"nlb_skh{k}", g) for k, g in enumerate(self.g_skh)]
+        out += [("S", self.g_u17), ("procrustes", self.g_u20), ("gram", self.g_u22), ("a1", self.g_a1),
+                ("a2", self.g_a2)]
+        return [(n, g) for n, g in out if g is not None]
 
     def launches_per_step(self, update=True):
-        n = 4 if True else 0
+        """Kernels of libpsgd_b200.so launched by one step (the RNG fill of the update uses torch's kernels)."""
+        n = 3  # prep, clip scale, apply
         groups = [self.g_a1, self.g_a2]
         if update:
+            n += 1 + 2 * int(self.nlb_spd_n > 0) + 2 + 2 * int(self.skew_n > 0)  # prep, nlb preps, factor x2, skew, rot
+            n -= int(self.skf_n == 0)
             groups += [self.g_u1, self.g_u2, self.g_u3, self.g_u10, self.g_u17, self.g_u20, self.g_u22]
             groups += self.g_spd + self.g_skh
-            n += 8
         return n + sum(g is not None for g in groups)
 
 
@@ -564,6 +581,7 @@ class KronWhiten:
         self._graphs = {}
         self._hyper_host = None
         self._steps = 0
+        self.trace = None  # optional callable(name) run after every launch (profiling; disables graphs)
         _capi.lib()  # fail loudly now if the kernels are missing
         if preconditioner_init_scale is not None:
             self._build(preconditioner_init_scale)
@@ -709,11 +727,21 @@ class KronWhiten:
             if update:
                 self._load_draws(draws["normals"])
 
+        trace = self.trace
+        if trace is not None:
+            use_graph = False  # launch-level CUDA events need eager launches
+            trace("start")
+
         def upd():
             if draws is None:
                 plan.xi.normal_()
                 plan.vbuf.normal_()
-            plan.run_update()
+                if trace is not None:
+                    trace("rng")
+            plan.run_update(trace)
+
+        def app():
+            plan.run_apply(trace)
 
         run = (lambda name, fn: self._phase(name, fn)) if use_graph else (lambda name, fn: fn())
         if update and self.update_preconditioner_first:
@@ -721,7 +749,7 @@ class KronWhiten:
             for k, c in enumerate(coins):
                 if c:
                     self._balance(k)
-        run("apply", plan.run_apply)
+        run("apply", app)
         if update and not self.update_preconditioner_first:
             run("update", upd)
             for k, c in enumerate(coins):
