@@ -28,6 +28,7 @@ extern "C" {
 #define PSGD_ELAUNCH -2    /* the CUDA launch itself failed */
 #define PSGD_ETMAP -3      /* the TMA descriptor could not be encoded */
 #define PSGD_ESPACE -4     /* a caller-provided table or workspace is too small */
+#define PSGD_ELIMIT -5     /* a size beyond the fixed scratch of psgd_apply_noalloc */
 
 /* ---------------------------------------------------------------------------------------------------------
  * Tensor-core GEMM: D = A * B^T (both operands K-major bf16 hi/lo, fp32 accumulation in TMEM), followed by a
@@ -199,6 +200,26 @@ typedef struct PsgdApplyItem {
 } PsgdApplyItem;
 int psgd_apply(const PsgdApplyItem* items, int nitems, const uint32_t* work, int nwork, const float* hyper,
                int* dev_err, cudaStream_t stream);
+
+/* Clip and apply for one parameter without any device memory from the caller. It has no counterpart in the
+ * reference, which always works through torch and so always allocates. It exists for callers that cannot
+ * allocate device memory: a plugin whose host application owns every device allocation, code that runs inside
+ * another framework's memory pool where a raw cudaMalloc is not allowed, or a latency-critical loop that cannot
+ * afford the device-wide synchronisation of cudaMalloc / cudaFree. The caller passes the parameter (fp32, or bf16
+ * when param_bf16 != 0; updated in place), its preconditioned gradient pg (fp32, numel values) and the three
+ * hyper-parameters by value; the result is that of psgd_apply: param -= lr_params * clamp(pg * min(1,
+ * max_avg_amp / rms(pg)), +-max_elem_amp).
+ * Scratch: one sum of squares per PSGD_APPLY_CHUNK elements, kept in a fixed 16 KB array inside the library that
+ * every GPU loading the library holds until the process exits. Limit: numel <= PSGD_APPLY_NOALLOC_MAX_NUMEL
+ * (33,554,432); larger parameters are rejected with PSGD_ELIMIT (use psgd_apply for them).
+ * The first call on a device looks up the array's device address with that device current; make that first call
+ * before any stream capture. All calls on a device share the array and leave their sums in it; each call writes
+ * every slot it reads before reading it, so nothing carries over, but calls whose kernels overlap on the GPU (on
+ * different streams) race on the array and produce wrong results. */
+#define PSGD_APPLY_NOALLOC_SLOTS 4096
+#define PSGD_APPLY_NOALLOC_MAX_NUMEL (4096LL * PSGD_APPLY_CHUNK)
+int psgd_apply_noalloc(void* param, int param_bf16, const float* pg, long long numel, float lr_params,
+                       float max_avg_amp, float max_elem_amp, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

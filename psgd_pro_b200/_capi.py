@@ -12,7 +12,8 @@ c_vp, c_ll, c_int, c_float = ctypes.c_void_p, ctypes.c_longlong, ctypes.c_int, c
 c_fp = ctypes.POINTER(ctypes.c_float)
 
 ERRORS = {-1: "invalid argument (shape, stride, alignment or mode)", -2: "CUDA launch failed",
-          -3: "TMA descriptor encoding failed", -4: "caller table or workspace too small"}
+          -3: "TMA descriptor encoding failed", -4: "caller table or workspace too small",
+          -5: "size beyond the fixed scratch of the no-allocation entry point"}
 
 PSGD_GEMM_PLAIN, PSGD_GEMM_SYRK = 0, 1
 
@@ -90,6 +91,7 @@ SIGNATURES = [
     ("psgd_skew", c_int, [c_vp, c_vp, c_int, c_vp, c_vp]),
     ("psgd_rot", c_int, [c_vp, c_vp, c_int, c_vp, c_vp]),
     ("psgd_apply", c_int, [c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_vp]),
+    ("psgd_apply_noalloc", c_int, [c_vp, c_int, c_vp, c_ll, c_float, c_float, c_float, c_vp]),
 ]
 
 _lib = None
