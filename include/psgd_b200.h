@@ -44,11 +44,14 @@ extern "C" {
  *   part_tile[tm * tiles_n + tn] = sum value^2 over the tile
  *   part_col[tm * N + c]         = sum over the tile's rows of value^2
  *   part_row[tn * M + r]         = sum over the tile's columns of value^2
- * mode PSGD_GEMM_SYRK: A == B, M == N, bn == 128; only tiles with tm <= tn run and the symmetric result is
- *   written to both triangles (element (r, c) with c >= r and its mirror), so the output is exactly symmetric.
- *   part_row then holds the row sums of squares of the full symmetric matrix, split over T = tiles_n slots
- *   (part_row[slot * M + r]); diag_out[r] = value(r, r); part_dot[tm * tiles_n + tn] = sum over the tile's share
- *   of the symmetric matrix of value * dot_aux (both triangles), i.e. sum_t part_dot = sum(S .* dot_aux).
+ * mode PSGD_GEMM_SYRK: A == B, M == N, bn 128 or 256; only the tiles that reach the upper triangle run (tile
+ *   (tm, tn) with tn >= tm * 128 / bn) and each element (r, c) with c >= r is written together with its mirror
+ *   (c, r), so the output is exactly symmetric. Reductions in this mode:
+ *   part_row[slot * M + r]: row sums of squares of the full symmetric matrix split over tiles_n + tiles_m slots
+ *     (slot tn: the direct elements of tile (tm, tn); slot tiles_n + tm: the mirrored ones); slots no tile writes
+ *     are never touched, so the buffer must start at zero once and the sum over all slots is the row sum;
+ *   diag_out[r] = value(r, r); part_dot[tm * tiles_n + tn] = the tile's share of sum(S .* dot_aux) over both
+ *     triangles (again zero-initialised once; the total is the sum of all entries).
  */
 #define PSGD_GEMM_PLAIN 0
 #define PSGD_GEMM_SYRK 1
@@ -150,7 +153,7 @@ int psgd_nlb_prep(const PsgdNlbPrepItem* items, int nitems, int* dev_err, cudaSt
  *   FACTOR_DIAG: term1_i = sum_s part[s * n + i]; ell = max term1 + term2; L as above;
  *         q_i *= 1 - lr/L (term1_i - term2); p_i = q_i^2.
  *   FACTOR_SKEW: s = nf * max_c ||W4_c|| + tiny (the skew bound of R = Q - Q^T); tr(RQ) = sum(part_dot_rq) / s,
- *         tr(RRQ) = -sum(part_dot_sq) / s^2; a = min(-tr(RQ)/tr(RRQ), 1/8) if tr(RRQ) < 0 else 1/8;
+ *         tr(RRQ) = -sum(part_dot_sq[0 .. n_sq)) / s^2; a = min(-tr(RQ)/tr(RRQ), 1/8) if tr(RRQ) < 0 else 1/8;
  *         *alpha = a, *beta = 1 / s   (the Procrustes step of psgd_pro_fast.py:141-153). */
 #define PSGD_FACTOR_DENSE 0
 #define PSGD_FACTOR_RANK1 1
@@ -163,7 +166,7 @@ typedef struct PsgdFactorItem {
   float* alpha; float* beta;
   float* q; float* p;
   const float* part_dot_rq; int n_rq;
-  const float* part_dot_sq; int tiles_sq;
+  const float* part_dot_sq; int n_sq;
 } PsgdFactorItem;
 int psgd_factor_update(const PsgdFactorItem* items, int nitems, const float* hyper, int* dev_err,
                        cudaStream_t stream);

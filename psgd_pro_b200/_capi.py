@@ -53,7 +53,7 @@ class NlbPrepItem(ctypes.Structure):
 class FactorItem(ctypes.Structure):
     _fields_ = [("kind", c_int), ("n", c_int), ("term2", c_float), ("L", c_vp), ("nf", c_vp), ("part", c_vp),
                 ("slots", c_int), ("ncols", c_int), ("alpha", c_vp), ("beta", c_vp), ("q", c_vp), ("p", c_vp),
-                ("part_dot_rq", c_vp), ("n_rq", c_int), ("part_dot_sq", c_vp), ("tiles_sq", c_int)]
+                ("part_dot_rq", c_vp), ("n_rq", c_int), ("part_dot_sq", c_vp), ("n_sq", c_int)]
 
 
 class SkewItem(ctypes.Structure):

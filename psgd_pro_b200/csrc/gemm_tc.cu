@@ -39,62 +39,67 @@ struct GemmCfg {
   static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
   static constexpr int TMEM_COLS = 2 * BNMAX;
   static constexpr int CTRL_BYTES = 256;  // barriers, TMEM slot, abort flag
-  static constexpr int RED_FLOATS = 4 * BNMAX + BNMAX + 32;
+  static constexpr int RED_FLOATS = 4 * BNMAX + BNMAX + 32 + 4 * 32 * 36;  // + the staging blocks
   static constexpr int SMEM_BYTES = 1024 + TILE_BYTES + CTRL_BYTES + RED_FLOATS * 4;
   static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
 };
 
 // ---- epilogue ------------------------------------------------------------------------------------------------
-// Stores `w` consecutive fp32 values of one row, vectorised when the run is 16-byte aligned and in range.
-PSGD_DEVI void store_row_f32(float* dst, const float* v, int w, int nvalid) {
-  if (nvalid == w && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
-#pragma unroll
-    for (int j = 0; j < 32; j += 4)
-      if (j < w) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+// Each epilogue warp owns 32 accumulator rows (its TMEM lane quadrant) and walks them in 32-column chunks. A chunk
+// is loaded from TMEM one row per lane, scaled by alpha and staged in a 32 x 36 shared-memory block (16-byte rows,
+// float4 traffic without bank conflicts), then read back in two layouts so every global access is a 16- or
+// 8-byte vector on contiguous addresses:
+//   column pass (lane = 4 columns of rows rs, rs+4, ...): aux term, row / column scales, row-major stores, row and
+//     column sums of squares, and for SYRK the direct (upper-triangle) stores, trace share and diagonal;
+//   transposed pass (lane = 4 consecutive rows of one column): transposed stores, and for SYRK the mirrored
+//     stores and the mirrored trace share.
+constexpr int STG = 36;  // staging pitch in floats
+
+PSGD_DEVI float4 ld4(const float* p, int n, bool vec) {
+  if (vec) return *reinterpret_cast<const float4*>(p);
+  float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (n > 0) r.x = p[0];
+  if (n > 1) r.y = p[1];
+  if (n > 2) r.z = p[2];
+  if (n > 3) r.w = p[3];
+  return r;
+}
+
+PSGD_DEVI void st4f(float* p, const float* x, int n, bool vec) {
+  if (vec) {
+    *reinterpret_cast<float4*>(p) = make_float4(x[0], x[1], x[2], x[3]);
   } else {
-    for (int j = 0; j < nvalid; ++j) dst[j] = v[j];
+    for (int i = 0; i < n; ++i) p[i] = x[i];
   }
 }
 
-PSGD_DEVI void store_row_bf16(__nv_bfloat16* hi, __nv_bfloat16* lo, const float* v, int w, int nvalid) {
-  if (nvalid == w && ((reinterpret_cast<uintptr_t>(hi) & 15) == 0) &&
-      (lo == nullptr || (reinterpret_cast<uintptr_t>(lo) & 15) == 0)) {
+PSGD_DEVI void st4b(__nv_bfloat16* hi, __nv_bfloat16* lo, const float* x, int n, bool vec) {
+  __align__(8) __nv_bfloat16 h[4], l[4];
 #pragma unroll
-    for (int j = 0; j < 32; j += 8) {
-      if (j < w) {
-        __align__(16) __nv_bfloat16 h[8], l[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) split_bf16(v[j + u], h[u], l[u]);
-        *reinterpret_cast<uint4*>(hi + j) = *reinterpret_cast<const uint4*>(h);
-        if (lo) *reinterpret_cast<uint4*>(lo + j) = *reinterpret_cast<const uint4*>(l);
-      }
-    }
+  for (int i = 0; i < 4; ++i) split_bf16(x[i], h[i], l[i]);
+  if (vec) {
+    *reinterpret_cast<uint2*>(hi) = *reinterpret_cast<const uint2*>(h);
+    if (lo) *reinterpret_cast<uint2*>(lo) = *reinterpret_cast<const uint2*>(l);
   } else {
-    for (int j = 0; j < nvalid; ++j) {
-      __nv_bfloat16 h, l;
-      split_bf16(v[j], h, l);
-      hi[j] = h;
-      if (lo) lo[j] = l;
+    for (int i = 0; i < n; ++i) {
+      hi[i] = h[i];
+      if (lo) lo[i] = l[i];
     }
   }
 }
 
 template <int BNMAX>
 __device__ void epilogue_tile(const GemmDesc& d, int tm, int tn, uint32_t tacc, int q, int lane, float* red,
-                              float* cs, float* misc) {
+                              float* cs, float* misc, float* stage) {
   const PsgdGemmSpec& s = d.s;
   const int bn = s.bn;
-  const int r = q * 32 + lane;  // tile row held by this thread (TMEM lane)
   const long long m0 = (long long)tm * BM, n0 = (long long)tn * bn;
-  const long long gr = m0 + r;
-  const bool rvalid = gr < s.M;
-  const int et = r;  // 0..127 among the epilogue threads
+  const long long row0 = m0 + q * 32;  // first row of this warp
+  const int et = q * 32 + lane;        // 0..127 among the epilogue threads
   const bool syrk = s.mode == PSGD_GEMM_SYRK;
-  const bool diag_tile = syrk && tm == tn;
 
   const float alpha = s.alpha * (s.alpha_ptr ? __ldg(s.alpha_ptr) : 1.f);
   const float beta = s.beta * (s.beta_ptr ? __ldg(s.beta_ptr) : 1.f);
-  const float rsc = (s.row_scale && rvalid) ? s.row_scale[gr] : 1.f;
   // Column scales. For the subspace products (cs_mode) the value is (D * 1/(|W_c| + tiny)) * 1/nf: two separate
   // multiplications in the reference's order (normalise V, then multiply by A / nf), so a zero matrix (nf = tiny)
   // gives zeros instead of 0 * inf.
@@ -116,10 +121,25 @@ __device__ void epilogue_tile(const GemmDesc& d, int tm, int tn, uint32_t tacc, 
       cs[c] = v;
     }
   }
-  const bool need_col = s.part_col != nullptr || (syrk && s.part_row != nullptr);
   named_sync(1, 128);
 
-  float tsum = 0.f, rsum = 0.f, dsum = 0.f;
+  const bool need_col = s.part_col != nullptr || (syrk && s.part_row != nullptr);
+  const bool tpass = syrk || s.out_hi_t != nullptr;
+  __nv_bfloat16* out_hi = (__nv_bfloat16*)s.out_hi;
+  __nv_bfloat16* out_lo = (__nv_bfloat16*)s.out_lo;
+  const bool vf32 = s.out_f32 && (s.ld_f32 % 4 == 0) && ((reinterpret_cast<uintptr_t>(s.out_f32) & 15) == 0);
+  const bool vb16 = out_hi && (s.ld_b % 4 == 0) && ((reinterpret_cast<uintptr_t>(out_hi) & 7) == 0) &&
+                    (!out_lo || (reinterpret_cast<uintptr_t>(out_lo) & 7) == 0);
+  const bool vaux = s.aux && (s.ld_aux % 4 == 0) && ((reinterpret_cast<uintptr_t>(s.aux) & 15) == 0);
+  const bool vdot = s.dot_aux && (s.ld_dot % 4 == 0) && ((reinterpret_cast<uintptr_t>(s.dot_aux) & 15) == 0);
+
+  // column-pass lane mapping: rows rs + 4 * it (it = 0..7), columns 4 * cg .. 4 * cg + 3 of the chunk
+  const int rs = lane >> 3, cg = lane & 7;
+  float rowacc[8];
+#pragma unroll
+  for (int it = 0; it < 8; ++it) rowacc[it] = 0.f;
+  float tsum = 0.f, dsum = 0.f;
+
   for (int c0 = 0; c0 < bn; c0 += 32) {
     float v[32];
     const int w = (bn - c0) >= 32 ? 32 : 16;
@@ -130,87 +150,165 @@ __device__ void epilogue_tile(const GemmDesc& d, int tm, int tn, uint32_t tacc, 
 #pragma unroll
       for (int j = 16; j < 32; ++j) v[j] = 0.f;
     }
-    const long long gc0 = n0 + c0;
-    int nvalid = 0;  // valid columns of this row in the chunk
-    if (rvalid) nvalid = (int)max(0LL, min((long long)w, (long long)s.N - gc0));
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      if (j < nvalid) {
-        float x = v[j] * alpha;
-        if (s.aux) x += beta * s.aux[gr * s.ld_aux + gc0 + j];
-        x *= rsc;
-        if (has_cs) x = (x * cs[c0 + j]) * inv_nf;
-        v[j] = x;
-      } else {
-        v[j] = 0.f;
+    for (int j = 0; j < 32; j += 4)
+      *reinterpret_cast<float4*>(stage + lane * STG + j) =
+          make_float4(v[j] * alpha, v[j + 1] * alpha, v[j + 2] * alpha, v[j + 3] * alpha);
+    __syncwarp();
+
+    // ---- column pass ----
+    const long long gcb = n0 + c0 + 4 * cg;
+    const int ncv = (4 * cg < w) ? (int)max(0LL, min(4LL, (long long)s.N - gcb)) : 0;
+    float csc[4] = {1.f, 1.f, 1.f, 1.f};
+    if (has_cs)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) csc[i] = (i < ncv) ? cs[c0 + 4 * cg + i] : 1.f;
+    float csq[4] = {0.f, 0.f, 0.f, 0.f};
+    float4 av[8];
+    if (s.aux) {  // issue every aux load of the chunk before using any
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const long long gr = row0 + rs + 4 * it;
+        av[it] = (gr < s.M && ncv > 0) ? ld4(s.aux + gr * s.ld_aux + gcb, ncv, vaux && ncv == 4)
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
-
-    if (!syrk) {
-      if (nvalid > 0) {
-        if (s.out_f32) store_row_f32(s.out_f32 + gr * s.ld_f32 + gc0, v, w, nvalid);
-        if (s.out_hi)
-          store_row_bf16((__nv_bfloat16*)s.out_hi + gr * s.ld_b + gc0,
-                         s.out_lo ? (__nv_bfloat16*)s.out_lo + gr * s.ld_b + gc0 : nullptr, v, w, nvalid);
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int r = rs + 4 * it;
+      const long long gr = row0 + r;
+      const bool rok = gr < s.M;
+      const float4 sv = *reinterpret_cast<const float4*>(stage + r * STG + 4 * cg);
+      float x[4] = {sv.x, sv.y, sv.z, sv.w};
+      if (s.aux) {
+        x[0] += beta * av[it].x;
+        x[1] += beta * av[it].y;
+        x[2] += beta * av[it].z;
+        x[3] += beta * av[it].w;
       }
-      if (s.out_hi_t) {  // transposed: consecutive lanes write consecutive rows (coalesced)
-        __nv_bfloat16* ht = (__nv_bfloat16*)s.out_hi_t;
-        __nv_bfloat16* lt = (__nv_bfloat16*)s.out_lo_t;
-        for (int j = 0; j < w; ++j) {
-          if (j < nvalid) {
-            __nv_bfloat16 h, l;
-            split_bf16(v[j], h, l);
-            ht[(gc0 + j) * s.ld_bt + gr] = h;
-            if (lt) lt[(gc0 + j) * s.ld_bt + gr] = l;
+      const float rsc = (s.row_scale && rok) ? s.row_scale[gr] : 1.f;
+      float rpart = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const bool ok = rok && i < ncv;
+        float xi = x[i] * rsc;
+        if (has_cs) xi = (xi * csc[i]) * inv_nf;
+        xi = ok ? xi : 0.f;
+        x[i] = xi;
+        const float x2 = xi * xi;
+        if (!syrk) {
+          rpart += x2;
+          csq[i] += x2;
+        } else {
+          const long long gc = gcb + i;
+          if (gc >= gr) rpart += x2;
+          if (gc > gr) csq[i] += x2;  // mirrored element (gc, gr) belongs to row gc
+          if (ok && gc == gr && s.diag_out) s.diag_out[gr] = xi;
+        }
+      }
+      tsum += rpart;
+      rowacc[it] += rpart;
+      if (rok && ncv > 0) {
+        if (!syrk) {
+          if (s.out_f32) st4f(s.out_f32 + gr * s.ld_f32 + gcb, x, ncv, vf32 && ncv == 4);
+          if (out_hi) st4b(out_hi + gr * s.ld_b + gcb, out_lo ? out_lo + gr * s.ld_b + gcb : nullptr, x, ncv,
+                           vb16 && ncv == 4);
+        } else {
+          const int first = (int)max(0LL, min(4LL, gr - gcb));  // elements i >= first have gc >= gr
+          if (first < ncv) {
+            const bool full = first == 0 && ncv == 4;
+            if (s.out_f32) {
+              if (full) st4f(s.out_f32 + gr * s.ld_f32 + gcb, x, 4, vf32);
+              else for (int i = first; i < ncv; ++i) s.out_f32[gr * s.ld_f32 + gcb + i] = x[i];
+            }
+            if (out_hi) {
+              if (full) {
+                st4b(out_hi + gr * s.ld_b + gcb, out_lo ? out_lo + gr * s.ld_b + gcb : nullptr, x, 4, vb16);
+              } else {
+                for (int i = first; i < ncv; ++i) {
+                  __nv_bfloat16 h, l;
+                  split_bf16(x[i], h, l);
+                  out_hi[gr * s.ld_b + gcb + i] = h;
+                  if (out_lo) out_lo[gr * s.ld_b + gcb + i] = l;
+                }
+              }
+            }
+            if (s.dot_aux) {
+              const float4 dv = ld4(s.dot_aux + gr * s.ld_dot + gcb, ncv, vdot && ncv == 4);
+              const float dd[4] = {dv.x, dv.y, dv.z, dv.w};
+              for (int i = first; i < ncv; ++i) dsum += x[i] * dd[i];
+            }
           }
         }
       }
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        tsum += v[j] * v[j];
-        rsum += v[j] * v[j];
-      }
-      if (s.part_col) {
-        float sq[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) sq[j] = v[j] * v[j];
-        red[q * BNMAX + c0 + lane] = warp_colsum32(sq, lane);
-      }
-    } else {
-      // symmetric output: (gr, gc) for gc >= gr and its mirror (gc, gr) for gc > gr
-      for (int j = 0; j < nvalid; ++j) {
-        const long long gc = gc0 + j;
-        if (gc < gr) continue;
-        __nv_bfloat16 h, l;
-        split_bf16(v[j], h, l);
-        if (s.out_f32) s.out_f32[gr * s.ld_f32 + gc] = v[j];
-        if (s.out_hi) ((__nv_bfloat16*)s.out_hi)[gr * s.ld_b + gc] = h;
-        if (s.out_lo) ((__nv_bfloat16*)s.out_lo)[gr * s.ld_b + gc] = l;
-        if (gc > gr) {
-          if (s.out_f32) s.out_f32[gc * s.ld_f32 + gr] = v[j];
-          if (s.out_hi) ((__nv_bfloat16*)s.out_hi)[gc * s.ld_b + gr] = h;
-          if (s.out_lo) ((__nv_bfloat16*)s.out_lo)[gc * s.ld_b + gr] = l;
-        }
-        if (s.diag_out && gc == gr) s.diag_out[gr] = v[j];
-        if (s.dot_aux) {
-          float dd = s.dot_aux[gr * s.ld_dot + gc];
-          if (gc > gr) dd += s.dot_aux[gc * s.ld_dot + gr];
-          dsum += v[j] * dd;
-        }
-      }
-      float sq[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const long long gc = gc0 + j;
-        const float x2 = v[j] * v[j];
-        rsum += (gc >= gr) ? x2 : 0.f;
-        sq[j] = (gc > gr) ? x2 : 0.f;
-      }
-      if (need_col) red[q * BNMAX + c0 + lane] = warp_colsum32(sq, lane);
+      *reinterpret_cast<float4*>(stage + r * STG + 4 * cg) = make_float4(x[0], x[1], x[2], x[3]);
     }
+    if (need_col) {  // column sums over the warp's 32 rows: reduce over the 4 lanes that share cg
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float t = csq[i];
+        t += __shfl_xor_sync(0xffffffffu, t, 8);
+        t += __shfl_xor_sync(0xffffffffu, t, 16);
+        csq[i] = t;
+      }
+      if (rs == 0)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) red[q * BNMAX + c0 + 4 * cg + i] = csq[i];
+    }
+    __syncwarp();
+
+    // ---- transposed pass: lane = rows 4 rg .. 4 rg + 3 of column 4 it + cs_ ----
+    if (tpass) {
+      const int cs_ = lane >> 3, rg = lane & 7;
+      const long long gr0 = row0 + 4 * rg;
+      const int nrv = (int)max(0LL, min(4LL, (long long)s.M - gr0));
+      __nv_bfloat16* ht = (__nv_bfloat16*)s.out_hi_t;
+      __nv_bfloat16* lt = (__nv_bfloat16*)s.out_lo_t;
+      const bool vt = ht && (s.ld_bt % 4 == 0) && ((reinterpret_cast<uintptr_t>(ht) & 7) == 0) &&
+                      (!lt || (reinterpret_cast<uintptr_t>(lt) & 7) == 0);
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int c = 4 * it + cs_;
+        const long long gc = n0 + c0 + c;
+        if (c >= w || gc >= s.N || nrv == 0) continue;
+        float x[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) x[i] = stage[(4 * rg + i) * STG + c];
+        if (!syrk) {
+          st4b(ht + gc * s.ld_bt + gr0, lt ? lt + gc * s.ld_bt + gr0 : nullptr, x, nrv, vt && nrv == 4);
+        } else {
+          // mirrors (gc, gr) of the elements with gc > gr: rows gr0 + i < gc
+          const int lim = (int)max(0LL, min((long long)nrv, gc - gr0));
+          if (lim > 0) {
+            const bool full = lim == 4;
+            if (s.out_f32) {
+              if (full) st4f(s.out_f32 + gc * s.ld_f32 + gr0, x, 4, vf32);
+              else for (int i = 0; i < lim; ++i) s.out_f32[gc * s.ld_f32 + gr0 + i] = x[i];
+            }
+            if (out_hi) st4b(out_hi + gc * s.ld_b + gr0, out_lo ? out_lo + gc * s.ld_b + gr0 : nullptr, x, lim,
+                             vb16 && full);
+            if (s.dot_aux) {
+              const float4 dv = ld4(s.dot_aux + gc * s.ld_dot + gr0, lim, vdot && full);
+              const float dd[4] = {dv.x, dv.y, dv.z, dv.w};
+              for (int i = 0; i < lim; ++i) dsum += x[i] * dd[i];
+            }
+          }
+        }
+      }
+    }
+    __syncwarp();
   }
 
   // ---- reductions over the 128 epilogue threads (fixed order) ----
+  // row sums: reduce over the 8 lanes that share rs (their 4-column partials)
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    float t = rowacc[it];
+    t += __shfl_xor_sync(0xffffffffu, t, 1);
+    t += __shfl_xor_sync(0xffffffffu, t, 2);
+    t += __shfl_xor_sync(0xffffffffu, t, 4);
+    rowacc[it] = t;
+  }
   if (s.part_tile || s.part_dot) {
     const float t1 = warp_sum(tsum), t2 = warp_sum(dsum);
     if (lane == 0) {
@@ -224,27 +322,23 @@ __device__ void epilogue_tile(const GemmDesc& d, int tm, int tn, uint32_t tacc, 
     if (s.part_tile) s.part_tile[tile_lin] = ((misc[0] + misc[1]) + misc[2]) + misc[3];
     if (s.part_dot) s.part_dot[tile_lin] = ((misc[4] + misc[5]) + misc[6]) + misc[7];
   }
-  if (!syrk) {
-    if (s.part_row && rvalid) s.part_row[(long long)tn * s.M + gr] = rsum;
-    if (s.part_col) {
-      for (int c = et; c < bn; c += 128) {
-        const long long gc = n0 + c;
-        if (gc < s.N) {
-          const float t = ((red[c] + red[BNMAX + c]) + red[2 * BNMAX + c]) + red[3 * BNMAX + c];
-          s.part_col[(long long)tm * s.N + gc] = t;
-        }
-      }
+  if (s.part_row && cg == 0) {  // direct share: slot tn
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const long long gr = row0 + rs + 4 * it;
+      if (gr < s.M) s.part_row[(long long)tn * s.M + gr] = rowacc[it];
     }
-  } else if (s.part_row) {
-    // column sums of the strict upper part are the mirrored rows' contributions
-    const int c = et;
-    const float colsum = ((red[c] + red[BNMAX + c]) + red[2 * BNMAX + c]) + red[3 * BNMAX + c];
-    if (diag_tile) {
-      if (rvalid) s.part_row[(long long)tn * s.M + gr] = rsum + colsum;
-    } else {
-      if (rvalid) s.part_row[(long long)tn * s.M + gr] = rsum;
-      const long long gc = n0 + c;
-      if (gc < s.N) s.part_row[(long long)tm * s.M + gc] = colsum;
+  }
+  if (need_col) {
+    for (int c = et; c < bn; c += 128) {
+      const long long gcc = n0 + c;
+      if (gcc >= s.N) continue;
+      const float t = ((red[c] + red[BNMAX + c]) + red[2 * BNMAX + c]) + red[3 * BNMAX + c];
+      if (!syrk) {
+        s.part_col[(long long)tm * s.N + gcc] = t;
+      } else {  // mirrored share of row gcc: slot tiles_n + tm
+        s.part_row[((long long)d.tiles_n + tm) * s.M + gcc] = t;
+      }
     }
   }
   named_sync(1, 128);  // red/cs/misc are reused by the next tile
@@ -261,14 +355,14 @@ PSGD_DEVI void get_tile(const GemmDesc* descs, const uint32_t* tiles, int t, int
   }
   p = 0;
   const GemmDesc& d = descs[0];
-  if (d.s.mode == PSGD_GEMM_SYRK) {
+  if (d.s.mode == PSGD_GEMM_SYRK) {  // row tm holds the tiles tn >= tm * BM / bn (they reach the upper triangle)
     int row = 0, rem = t;
-    while (rem >= d.tiles_n - row) {
-      rem -= d.tiles_n - row;
+    while (rem >= d.tiles_n - row * BM / d.s.bn) {
+      rem -= d.tiles_n - row * BM / d.s.bn;
       ++row;
     }
     tm = row;
-    tn = row + rem;
+    tn = row * BM / d.s.bn + rem;
   } else {
     tm = t / d.tiles_n;
     tn = t % d.tiles_n;
@@ -293,6 +387,7 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
   float* cs = red + 4 * BNMAX;
   float* misc = cs + BNMAX;
   volatile int* epi_ok = reinterpret_cast<volatile int*>(misc + 16);
+  float* stage_all = misc + 32;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -421,7 +516,7 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
       if (!all_ok) break;
       tc_fence_after();
       const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BNMAX;
-      epilogue_tile<BNMAX>(d, tm, tn, tacc, q, lane, red, cs, misc);
+      epilogue_tile<BNMAX>(d, tm, tn, tacc, q, lane, red, cs, misc, stage_all + q * 32 * STG);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -494,7 +589,7 @@ static int check_spec(const PsgdGemmSpec& s, int split) {
   if (split != 1 && split != 3) return PSGD_EINVAL;
   if (s.M < 1 || s.N < 1 || s.K < 1 || !valid_bn(s.bn, split)) return PSGD_EINVAL;
   if (split == 3 && (s.a_lo == nullptr || s.b_lo == nullptr)) return PSGD_EINVAL;
-  if (s.mode == PSGD_GEMM_SYRK && (s.M != s.N || s.bn != 128)) return PSGD_EINVAL;
+  if (s.mode == PSGD_GEMM_SYRK && (s.M != s.N || s.bn < 128)) return PSGD_EINVAL;
   if (s.mode != PSGD_GEMM_PLAIN && s.mode != PSGD_GEMM_SYRK) return PSGD_EINVAL;
   if (s.cs_mode && (s.cs_nf == nullptr || (s.cs_mode == 2 && (s.cs_part == nullptr || s.cs_T < 1)))) return PSGD_EINVAL;
   if (s.M > 65535 * BM || s.N > 65535 * s.bn) return PSGD_EINVAL;
@@ -522,14 +617,18 @@ static int fill_desc(GemmDesc* d, const PsgdGemmSpec& s, int split) {
 
 static int spec_tiles(const PsgdGemmSpec& s) {
   const int tmn = (s.M + BM - 1) / BM, tnn = (s.N + s.bn - 1) / s.bn;
-  if (s.mode == PSGD_GEMM_SYRK) return tmn * (tmn + 1) / 2;
+  if (s.mode == PSGD_GEMM_SYRK) {
+    int n = 0;
+    for (int tm = 0; tm < tmn; ++tm) n += tnn - tm * BM / s.bn;
+    return n;
+  }
   return tmn * tnn;
 }
 
 static void append_tiles(const PsgdGemmSpec& s, uint32_t p, uint32_t* out, int& k) {
   const int tmn = (s.M + BM - 1) / BM, tnn = (s.N + s.bn - 1) / s.bn;
   for (int tm = 0; tm < tmn; ++tm)
-    for (int tn = (s.mode == PSGD_GEMM_SYRK ? tm : 0); tn < tnn; ++tn) {
+    for (int tn = (s.mode == PSGD_GEMM_SYRK ? tm * BM / s.bn : 0); tn < tnn; ++tn) {
       out[2 * k] = p;
       out[2 * k + 1] = ((uint32_t)tm << 16) | (uint32_t)tn;
       ++k;

@@ -271,11 +271,7 @@ __global__ void __launch_bounds__(FAC_THREADS) factor_kernel(const PsgdFactorIte
     for (int t = threadIdx.x; t < it.n_rq; t += blockDim.x) a1 += it.part_dot_rq[t];
     const float sum_rq = block_sum(a1, red);
     float a2 = 0.f;
-    const int T = it.tiles_sq;
-    for (int t = threadIdx.x; t < T * T; t += blockDim.x) {
-      const int tm = t / T, tn = t % T;
-      if (tm <= tn) a2 += it.part_dot_sq[t];
-    }
+    for (int t = threadIdx.x; t < it.n_sq; t += blockDim.x) a2 += it.part_dot_sq[t];
     const float sum_sq = block_sum(a2, red);
     if (threadIdx.x == 0) {
       // divide step by step, as the reference normalises R before its products: with R = 0 (Q exactly

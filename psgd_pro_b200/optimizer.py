@@ -92,14 +92,17 @@ class _Factor:
             self.P, self.T, self.R = K.operand(n, n, dev, sp), K.operand(n, n, dev, sp), K.operand(n, n, dev, sp)
             self.V0, self.Wa, self.Wb = (K.operand(K_SUB, n, dev, sp) for _ in range(3))
             self.Tn, self.T32 = cdiv(n, BM), cdiv(n, TT)
-            self.t_rows = torch.zeros(self.Tn, n, device=dev)
+            # SYRK tiles are 128 x sbn; its row-sum partials use cdiv(n, sbn) direct + Tn mirrored slots
+            self.sbn = 256 if split == 1 else 128
+            self.Ts = cdiv(n, self.sbn) + self.Tn
+            self.t_rows = torch.zeros(self.Ts, n, device=dev)
             self.t_diag = torch.zeros(n, device=dev)
             self.pc = torch.zeros(4, self.Tn, K_SUB, device=dev)
             self.pcs = torch.zeros(4, self.Tn, K_SUB, device=dev)
             self.r_rows = torch.zeros(self.T32, n, device=dev)
             self.r_max = torch.zeros(self.T32 * self.T32, device=dev)
             self.r_dot = torch.zeros(self.T32 * self.T32, device=dev)
-            self.s_dot = torch.zeros(self.Tn * self.Tn, device=dev)
+            self.s_dot = torch.zeros(self.Tn * cdiv(n, self.sbn), device=dev)
             self.refresh_operands()
         elif kind == "diag":
             self.q = torch.full((n,), float(scale), device=dev)
@@ -200,7 +203,7 @@ class _Plan:
         return K.make_spec(a, b, M, N, Kd, bn=bn or choose_bn(N, self.split), **kw)
 
     def syrk(self, a, n, Kd, **kw):
-        return K.make_spec(a, a, n, n, Kd, bn=128, mode=K.PSGD_GEMM_SYRK, **kw)
+        return K.make_spec(a, a, n, n, Kd, bn=256 if self.split == 1 else 128, mode=K.PSGD_GEMM_SYRK, **kw)
 
     def group(self, specs):
         if not specs:
@@ -347,7 +350,7 @@ class _Plan:
             it.kind, it.n, it.nf, it.part, it.slots, it.ncols = (PSGD_FACTOR_SKEW, f.n, self.s(f, S_NF_SKH).data_ptr(),
                                                                 f.pcs[3].data_ptr(), f.Tn, K_SUB)
             it.part_dot_rq, it.n_rq = f.r_dot.data_ptr(), f.r_dot.numel()
-            it.part_dot_sq, it.tiles_sq = f.s_dot.data_ptr(), f.Tn
+            it.part_dot_sq, it.n_sq = f.s_dot.data_ptr(), f.s_dot.numel()
             it.alpha, it.beta = self.s(f, S_AM).data_ptr(), self.s(f, S_BM).data_ptr()
             si.append(it)
         self.skf_dev, self.skf_n = _upload(_capi.FactorItem, si, dev), len(si)
@@ -411,7 +414,7 @@ class _Plan:
                 it.v = f.v_skh.data_ptr()
                 it.nf_out = self.s(f, S_NF_SKH).data_ptr()
             else:
-                it.part_row, it.row_slots, it.diag = f.t_rows.data_ptr(), f.Tn, f.t_diag.data_ptr()
+                it.part_row, it.row_slots, it.diag = f.t_rows.data_ptr(), f.Ts, f.t_diag.data_ptr()
                 it.v = f.v_spd.data_ptr()
                 it.nf_out = self.s(f, S_NF_SPD).data_ptr()
             it.v0_hi, it.v0_lo, it.ldv = K.ptr(f.V0[0]), K.ptr(f.V0[1]), f.V0[0].stride(0)

@@ -57,19 +57,20 @@ def test_split_fp32(cuda, M, N, Kd, bn):
     assert rel(out1, ref) > 10 * rel(out, ref)
 
 
-@pytest.mark.parametrize("n,Kd,split", [(128, 64, 1), (384, 200, 3), (300, 1000, 1), (10, 7, 3)])
-def test_syrk_symmetric(cuda, n, Kd, split):
+@pytest.mark.parametrize("n,Kd,split,bn", [(128, 64, 1, 128), (384, 200, 3, 128), (300, 1000, 1, 128),
+                                          (10, 7, 3, 128), (600, 300, 1, 256), (1030, 64, 1, 256), (256, 96, 1, 256)])
+def test_syrk_symmetric(cuda, n, Kd, split, bn):
     g = torch.Generator().manual_seed(n)
     x, X = bf16_operand(n, Kd, cuda, g, split=split == 3)
-    T = (n + 127) // 128
+    Tm, Tn = (n + 127) // 128, (n + bn - 1) // bn
     out = torch.full((n, n), float("nan"), device=cuda)
     hi, lo = K.operand(n, n, cuda, split=split == 3)
-    part_row = torch.full((T, n), float("nan"), device=cuda)
+    part_row = torch.zeros(Tn + Tm, n, device=cuda)  # zero once: slots no tile reaches stay zero
     diag = torch.empty(n, device=cuda)
     dot_aux = torch.randn(n, n, generator=g).to(cuda)
-    part_dot = torch.zeros(T * T, device=cuda)
+    part_dot = torch.zeros(Tm * Tn, device=cuda)
     err = err_word(cuda)
-    spec = K.make_spec(X, X, n, n, Kd, bn=128, mode=K.PSGD_GEMM_SYRK, out_f32=out, out_hi=hi, out_lo=lo,
+    spec = K.make_spec(X, X, n, n, Kd, bn=bn, mode=K.PSGD_GEMM_SYRK, out_f32=out, out_hi=hi, out_lo=lo,
                        part_row=part_row, diag_out=diag, dot_aux=dot_aux, part_dot=part_dot)
     K.gemm(spec, split, err)
     torch.cuda.synchronize()
@@ -81,7 +82,7 @@ def test_syrk_symmetric(cuda, n, Kd, split):
     assert rel(hi[:, :n].float(), ref) < 1e-2
     assert rel(part_row.sum(0), (ref ** 2).sum(1)) < 1e-4
     assert rel(diag, ref.diagonal()) < 2e-5
-    got_dot = sum(part_dot[tm * T + tn].item() for tm in range(T) for tn in range(tm, T))
+    got_dot = part_dot.double().sum().item()
     want = (ref * dot_aux.double()).sum().item()
     assert abs(got_dot - want) <= 1e-4 * (ref.abs() * dot_aux.double().abs()).sum().item()
 
