@@ -36,6 +36,13 @@ def llama_1b():
     return s
 
 
+def llama_layer():
+    """One decoder layer of the Llama-style set (the same factor sizes 256, 2048 and 5632): a small case of the
+    1.1 B workload for profiling, 9 tensors, 44 M parameters."""
+    d, f, kv = 2048, 5632, 256
+    return [(d, d), (kv, d), (kv, d), (d, d), (f, d), (f, d), (d, f), (d,), (d,)]
+
+
 def config1():
     """One fp32 256 x 512 weight (the reference CPU case)."""
     return [(256, 512)]
@@ -44,6 +51,7 @@ def config1():
 WORKLOADS = {
     # name: (shapes, parameter dtype, gradient dtype, gradient std, description)
     "llama-1.1b": (llama_1b, "bf16", "bf16", 1e-3, "Llama-style 1.1B parameter set, bf16 params/grads, fp32 Q"),
+    "llama-layer": (llama_layer, "bf16", "bf16", 1e-3, "one decoder layer of the Llama-style set (profiling case)"),
     "gpt2-medium": (gpt2_medium, "bf16", "bf16", 1e-3, "GPT-2-medium parameter set, bf16 params/grads, fp32 Q"),
     "vit-tiny": (vit_tiny, "fp32", "bf16", 1e-3, "ViT-Tiny parameter set, fp32 params, bf16 grads"),
     "config1": (config1, "fp32", "fp32", 1e-2, "one fp32 256x512 weight"),
