@@ -81,13 +81,15 @@ int psgd_gemm(const PsgdGemmSpec* spec, int split, int* dev_err, cudaStream_t st
 
 /* Grouped form: encode once on the host into caller buffers, copy the table and tile list to the device, then
  * launch any number of times (the launch reads only device memory, so it can be captured in a CUDA graph).
- * Tiles run in the order the specs are given (callers put the costliest problems first). */
+ * Tiles run in the order the specs are given (callers put the costliest problems first). Encoding also reports
+ * the group's epilogue kind (*kind, 0..4), which the launch takes back: interior tiles of the problems of that
+ * kind run a specialised epilogue, all other tiles the general one. */
 size_t psgd_gemm_table_bytes(int nspecs);
 int psgd_gemm_count_tiles(const PsgdGemmSpec* specs, int nspecs);
 int psgd_gemm_encode(const PsgdGemmSpec* specs, int nspecs, void* host_table, size_t table_bytes,
-                     uint32_t* host_tiles, int max_tiles, int* ntiles);
-int psgd_gemm_launch(const void* dev_table, const uint32_t* dev_tiles, int ntiles, int split, int* dev_err,
-                     cudaStream_t stream);
+                     uint32_t* host_tiles, int max_tiles, int* ntiles, int* kind);
+int psgd_gemm_launch(const void* dev_table, const uint32_t* dev_tiles, int ntiles, int split, int kind,
+                     int* dev_err, cudaStream_t stream);
 
 /* Number of SMs the grouped launches use on the current device (grid size of the persistent kernels). */
 int psgd_num_sms(void);
@@ -112,7 +114,10 @@ int psgd_num_sms(void);
  *   PREP_TRANS:  out (n2 x n1, bf16 hi/lo)           = (x * p2[j])^T
  *   PREP_DIRECT: out_f32 (n1 x n2) = p1[i] x p2[j]   (both factors diagonal: the whole preconditioned gradient)
  *               with optional part_row[tj][i], part_col[ti][j], part_tile[ti * tiles_j + tj] sums of squares.
- * p1/p2 NULL mean ones. Replaces the exprP prologue of psgd_pro.py:123 and psgd_pro_fast.py:176. */
+ * p1/p2 NULL mean ones. Work entries: (item, row block of PSGD_PREP_ROWS rows) for PREP_NORMAL, (item,
+ * (ti << 16) | tj) 32 x 32 tiles otherwise. Replaces the exprP prologue of psgd_pro.py:123 and
+ * psgd_pro_fast.py:176. */
+#define PSGD_PREP_ROWS 8   /* PREP_NORMAL work entries cover PSGD_PREP_ROWS rows: (item, row block) */
 #define PSGD_PREP_NORMAL 0
 #define PSGD_PREP_TRANS 1
 #define PSGD_PREP_DIRECT 2
@@ -171,9 +176,10 @@ typedef struct PsgdFactorItem {
 int psgd_factor_update(const PsgdFactorItem* items, int nitems, const float* hyper, int* dev_err,
                        cudaStream_t stream);
 
-/* Rn = Q - Q^T on 32 x 32 tiles of an n x n fp32 Q (psgd_pro_fast.py:147; psgd_pro.py:87 up to sign), written
- * as bf16 hi/lo, with part_row[tj][i] (row sums of squares), part_max[tile] (max |Rn|) and part_dot[tile]
- * (sum Rn * Q) for tile = ti * tiles + tj. */
+/* Rn = Q - Q^T (psgd_pro_fast.py:147; psgd_pro.py:87 up to sign), written as bf16 hi/lo. Work entries are
+ * 32 x 32 tile pairs (ti <= tj): one block reads Q[ti, tj] and Q[tj, ti] once and writes both Rn tiles, with
+ * part_row[slot][i] (row sums of squares; the slot is the column tile), and per pair part_max (max |Rn|) and
+ * part_dot (sum Rn * Q) in entry ti * tiles + tj (entries with ti > tj stay zero). */
 typedef struct PsgdSkewItem {
   const float* q; int n;
   void* r_hi; void* r_lo; long long ldr;
@@ -181,8 +187,9 @@ typedef struct PsgdSkewItem {
 } PsgdSkewItem;
 int psgd_skew(const PsgdSkewItem* items, const uint32_t* work, int nwork, int* dev_err, cudaStream_t stream);
 
-/* M = a (Rn / s) + a^2 / 2 ((S / s) / s) on 32 x 32 tiles (bf16 hi/lo in, bf16 hi/lo out in place of Rn), with
- * a = *alpha and 1/s = *beta from PSGD_FACTOR_SKEW: the Procrustes multiplier of psgd_pro_fast.py:153. */
+/* M = a (Rn / s) + a^2 / 2 ((S / s) / s) (bf16 hi/lo in, bf16 hi/lo out in place of Rn), with a = *alpha and
+ * 1/s = *beta from PSGD_FACTOR_SKEW: the Procrustes multiplier of psgd_pro_fast.py:153. Work entries: (item,
+ * first row of a block of 4 rows); whole padded rows are processed (padding columns are zero and stay zero). */
 typedef struct PsgdRotItem {
   int n;
   void* r_hi; void* r_lo; long long ldr;
@@ -203,6 +210,24 @@ typedef struct PsgdApplyItem {
 } PsgdApplyItem;
 int psgd_apply(const PsgdApplyItem* items, int nitems, const uint32_t* work, int nwork, const float* hyper,
                int* dev_err, cudaStream_t stream);
+
+/* Factor balancing of the listed parameters (psgd_pro.py:96-105, drawn with probability 0.01 per parameter):
+ * max |q| of each factor (absmax over work_max entries (factor, chunk of PSGD_APPLY_CHUNK values) into part),
+ * c_k = (prod_k max_k)^(1/order) / max_k per parameter (into *scale), then work_apply entries rescale: dense
+ * factors per 32 x 32 tile (factor, (ti << 16) | tj): Q *= c, Q^T rewritten from the new Q, P *= c^2; diagonal
+ * factors per chunk (factor, chunk): q *= c, p = q^2. part and scale are caller scratch. */
+typedef struct PsgdBalanceFactor {
+  float* q; int n; int dense;
+  void* qt_hi; void* qt_lo; long long ldqt;
+  void* p_hi; void* p_lo; long long ldp;
+  float* pdiag;
+  float* part; int nparts;
+  float* scale;
+} PsgdBalanceFactor;
+typedef struct PsgdBalanceParam { int f0; int nf; } PsgdBalanceParam;
+int psgd_balance(const PsgdBalanceFactor* factors, const PsgdBalanceParam* params, int nparams,
+                 const uint32_t* work_max, int nwork_max, const uint32_t* work_apply, int nwork_apply, int* dev_err,
+                 cudaStream_t stream);
 
 /* Clip and apply for one parameter without any device memory from the caller. It has no counterpart in the
  * reference, which always works through torch and so always allocates. It exists for callers that cannot

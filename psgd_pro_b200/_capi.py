@@ -71,7 +71,18 @@ class ApplyItem(ctypes.Structure):
                 ("nparts", c_int), ("scale", c_vp)]
 
 
+class BalanceFactor(ctypes.Structure):
+    _fields_ = [("q", c_vp), ("n", c_int), ("dense", c_int), ("qt_hi", c_vp), ("qt_lo", c_vp), ("ldqt", c_ll),
+                ("p_hi", c_vp), ("p_lo", c_vp), ("ldp", c_ll), ("pdiag", c_vp), ("part", c_vp), ("nparts", c_int),
+                ("scale", c_vp)]
+
+
+class BalanceParam(ctypes.Structure):
+    _fields_ = [("f0", c_int), ("nf", c_int)]
+
+
 PSGD_PREP_NORMAL, PSGD_PREP_TRANS, PSGD_PREP_DIRECT = 0, 1, 2
+PREP_ROWS = 8
 PSGD_FACTOR_DENSE, PSGD_FACTOR_RANK1, PSGD_FACTOR_DIAG, PSGD_FACTOR_SKEW = 0, 1, 2, 3
 HY_LR_PRECOND, HY_BETA_L, HY_DAMPING, HY_LR_PARAMS, HY_MAX_AVG, HY_MAX_ELEM, HY_MOM_BETA, HY_COUNT = range(8)
 APPLY_CHUNK = 8192
@@ -83,14 +94,15 @@ SIGNATURES = [
     ("psgd_gemm_table_bytes", ctypes.c_size_t, [c_int]),
     ("psgd_gemm_count_tiles", c_int, [ctypes.POINTER(GemmSpec), c_int]),
     ("psgd_gemm_encode", c_int, [ctypes.POINTER(GemmSpec), c_int, c_vp, ctypes.c_size_t, c_vp, c_int,
-                                 ctypes.POINTER(c_int)]),
-    ("psgd_gemm_launch", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp]),
+                                 ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
+    ("psgd_gemm_launch", c_int, [c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp]),
     ("psgd_prep", c_int, [c_vp, c_vp, c_int, c_vp, c_vp, c_vp]),
     ("psgd_nlb_prep", c_int, [c_vp, c_int, c_vp, c_vp]),
     ("psgd_factor_update", c_int, [c_vp, c_int, c_vp, c_vp, c_vp]),
     ("psgd_skew", c_int, [c_vp, c_vp, c_int, c_vp, c_vp]),
     ("psgd_rot", c_int, [c_vp, c_vp, c_int, c_vp, c_vp]),
     ("psgd_apply", c_int, [c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_vp]),
+    ("psgd_balance", c_int, [c_vp, c_vp, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_vp]),
     ("psgd_apply_noalloc", c_int, [c_vp, c_int, c_vp, c_ll, c_float, c_float, c_float, c_vp]),
 ]
 

@@ -28,6 +28,7 @@ struct __align__(64) GemmDesc {
   CUtensorMap tb[2];  // B hi, lo
   PsgdGemmSpec s;
   int tiles_m, tiles_n;
+  int fast;  // EPI_* kind of the fast epilogue for interior tiles (0: generic only)
 };
 
 template <int SPLIT, int BNMAX, int STAGES>
@@ -65,56 +66,104 @@ PSGD_DEVI float4 ld4(const float* p, int n, bool vec) {
   return r;
 }
 
+// Tails use fully unrolled, predicated loops: a runtime index into x would force the value arrays into local
+// memory for the whole hot loop.
 PSGD_DEVI void st4f(float* p, const float* x, int n, bool vec) {
   if (vec) {
     *reinterpret_cast<float4*>(p) = make_float4(x[0], x[1], x[2], x[3]);
   } else {
-    for (int i = 0; i < n; ++i) p[i] = x[i];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (i < n) p[i] = x[i];
   }
 }
 
+PSGD_DEVI uint32_t pack_bf16x2(__nv_bfloat16 a, __nv_bfloat16 b) {
+  return (uint32_t)__bfloat16_as_ushort(a) | ((uint32_t)__bfloat16_as_ushort(b) << 16);
+}
+
+// Four values as bf16 hi (and lo) at hi[0..3] / lo[0..3]; one 8-byte store each when vec.
 PSGD_DEVI void st4b(__nv_bfloat16* hi, __nv_bfloat16* lo, const float* x, int n, bool vec) {
-  __align__(8) __nv_bfloat16 h[4], l[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) split_bf16(x[i], h[i], l[i]);
+  __nv_bfloat16 h0, h1, h2, h3, l0, l1, l2, l3;
+  split_bf16(x[0], h0, l0);
+  split_bf16(x[1], h1, l1);
+  split_bf16(x[2], h2, l2);
+  split_bf16(x[3], h3, l3);
   if (vec) {
-    *reinterpret_cast<uint2*>(hi) = *reinterpret_cast<const uint2*>(h);
-    if (lo) *reinterpret_cast<uint2*>(lo) = *reinterpret_cast<const uint2*>(l);
+    *reinterpret_cast<uint2*>(hi) = make_uint2(pack_bf16x2(h0, h1), pack_bf16x2(h2, h3));
+    if (lo) *reinterpret_cast<uint2*>(lo) = make_uint2(pack_bf16x2(l0, l1), pack_bf16x2(l2, l3));
   } else {
-    for (int i = 0; i < n; ++i) {
-      hi[i] = h[i];
-      if (lo) lo[i] = l[i];
+    if (n > 0) hi[0] = h0;
+    if (n > 1) hi[1] = h1;
+    if (n > 2) hi[2] = h2;
+    if (n > 3) hi[3] = h3;
+    if (lo) {
+      if (n > 0) lo[0] = l0;
+      if (n > 1) lo[1] = l1;
+      if (n > 2) lo[2] = l2;
+      if (n > 3) lo[3] = l3;
     }
   }
 }
 
 template <int BNMAX>
-__device__ void epilogue_tile(const GemmDesc& d, int tm, int tn, uint32_t tacc, int q, int lane, float* red,
+__device__ __forceinline__ void epilogue_tile(const GemmDesc& d, int tm, int tn, uint32_t tacc, int q, int lane, float* red,
                               float* cs, float* misc, float* stage) {
-  const PsgdGemmSpec& s = d.s;
-  const int bn = s.bn;
+  // Every descriptor field the loops use is copied into a register first: the staging stores go through
+  // pointers the compiler cannot separate from the descriptor, so reading d.s.* inside the loops would reload
+  // each field from memory on every iteration.
+  const PsgdGemmSpec& sd = d.s;
+  const long long s_M = sd.M, s_N = sd.N;
+  const float* __restrict__ s_aux = sd.aux;
+  const long long s_ld_aux = sd.ld_aux;
+  const float* __restrict__ s_row_scale = sd.row_scale;
+  const float* __restrict__ s_col_scale = sd.col_scale;
+  float* __restrict__ s_out_f32 = sd.out_f32;
+  const long long s_ld_f32 = sd.ld_f32;
+  void* s_out_hi = sd.out_hi;
+  void* s_out_lo = sd.out_lo;
+  const long long s_ld_b = sd.ld_b;
+  void* s_out_hi_t = sd.out_hi_t;
+  void* s_out_lo_t = sd.out_lo_t;
+  const long long s_ld_bt = sd.ld_bt;
+  float* __restrict__ s_part_tile = sd.part_tile;
+  float* __restrict__ s_part_col = sd.part_col;
+  float* __restrict__ s_part_row = sd.part_row;
+  float* __restrict__ s_diag_out = sd.diag_out;
+  const float* __restrict__ s_dot_aux = sd.dot_aux;
+  const long long s_ld_dot = sd.ld_dot;
+  float* __restrict__ s_part_dot = sd.part_dot;
+  const float* __restrict__ s_cs_part = sd.cs_part;
+  const int s_cs_T = sd.cs_T, s_cs_mode = sd.cs_mode, s_mode = sd.mode, s_bn = sd.bn;
+  const float* s_cs_nf = sd.cs_nf;
+  const float s_alpha = sd.alpha, s_beta = sd.beta;
+  const float* s_alpha_ptr = sd.alpha_ptr;
+  const float* s_beta_ptr = sd.beta_ptr;
+  const int d_tiles_n = d.tiles_n;
+
+  const int bn = s_bn;
   const long long m0 = (long long)tm * BM, n0 = (long long)tn * bn;
   const long long row0 = m0 + q * 32;  // first row of this warp
   const int et = q * 32 + lane;        // 0..127 among the epilogue threads
-  const bool syrk = s.mode == PSGD_GEMM_SYRK;
+  const bool syrk = s_mode == PSGD_GEMM_SYRK;
 
-  const float alpha = s.alpha * (s.alpha_ptr ? __ldg(s.alpha_ptr) : 1.f);
-  const float beta = s.beta * (s.beta_ptr ? __ldg(s.beta_ptr) : 1.f);
+  const float alpha = s_alpha * (s_alpha_ptr ? __ldg(s_alpha_ptr) : 1.f);
+  const float beta = s_beta * (s_beta_ptr ? __ldg(s_beta_ptr) : 1.f);
   // Column scales. For the subspace products (cs_mode) the value is (D * 1/(|W_c| + tiny)) * 1/nf: two separate
   // multiplications in the reference's order (normalise V, then multiply by A / nf), so a zero matrix (nf = tiny)
   // gives zeros instead of 0 * inf.
-  const bool has_cs = s.col_scale != nullptr || s.cs_mode != 0;
-  const float inv_nf = s.cs_mode ? 1.f / *s.cs_nf : 1.f;
+  const bool has_cs = s_col_scale != nullptr || s_cs_mode != 0;
+  const float inv_nf = s_cs_mode ? 1.f / *s_cs_nf : 1.f;
   if (has_cs) {
     for (int c = et; c < bn; c += 128) {
       const long long gc = n0 + c;
       float v = 1.f;
-      if (gc < s.N) {
-        if (s.col_scale) {
-          v = s.col_scale[gc];
-        } else if (s.cs_mode == 2) {
+      if (gc < s_N) {
+        if (s_col_scale) {
+          v = s_col_scale[gc];
+        } else if (s_cs_mode == 2) {
           float acc = 0.f;
-          for (int t = 0; t < s.cs_T; ++t) acc += s.cs_part[(long long)t * s.N + gc];
+          for (int t = 0; t < s_cs_T; ++t) acc += s_cs_part[(long long)t * s_N + gc];
           v = 1.f / (sqrtf(acc) + FLT_MIN);
         }
       }
@@ -123,15 +172,15 @@ __device__ void epilogue_tile(const GemmDesc& d, int tm, int tn, uint32_t tacc, 
   }
   named_sync(1, 128);
 
-  const bool need_col = s.part_col != nullptr || (syrk && s.part_row != nullptr);
-  const bool tpass = syrk || s.out_hi_t != nullptr;
-  __nv_bfloat16* out_hi = (__nv_bfloat16*)s.out_hi;
-  __nv_bfloat16* out_lo = (__nv_bfloat16*)s.out_lo;
-  const bool vf32 = s.out_f32 && (s.ld_f32 % 4 == 0) && ((reinterpret_cast<uintptr_t>(s.out_f32) & 15) == 0);
-  const bool vb16 = out_hi && (s.ld_b % 4 == 0) && ((reinterpret_cast<uintptr_t>(out_hi) & 7) == 0) &&
+  const bool need_col = s_part_col != nullptr || (syrk && s_part_row != nullptr);
+  const bool tpass = syrk || s_out_hi_t != nullptr;
+  __nv_bfloat16* out_hi = (__nv_bfloat16*)s_out_hi;
+  __nv_bfloat16* out_lo = (__nv_bfloat16*)s_out_lo;
+  const bool vf32 = s_out_f32 && (s_ld_f32 % 4 == 0) && ((reinterpret_cast<uintptr_t>(s_out_f32) & 15) == 0);
+  const bool vb16 = out_hi && (s_ld_b % 4 == 0) && ((reinterpret_cast<uintptr_t>(out_hi) & 7) == 0) &&
                     (!out_lo || (reinterpret_cast<uintptr_t>(out_lo) & 7) == 0);
-  const bool vaux = s.aux && (s.ld_aux % 4 == 0) && ((reinterpret_cast<uintptr_t>(s.aux) & 15) == 0);
-  const bool vdot = s.dot_aux && (s.ld_dot % 4 == 0) && ((reinterpret_cast<uintptr_t>(s.dot_aux) & 15) == 0);
+  const bool vaux = s_aux && (s_ld_aux % 4 == 0) && ((reinterpret_cast<uintptr_t>(s_aux) & 15) == 0);
+  const bool vdot = s_dot_aux && (s_ld_dot % 4 == 0) && ((reinterpret_cast<uintptr_t>(s_dot_aux) & 15) == 0);
 
   // column-pass lane mapping: rows rs + 4 * it (it = 0..7), columns 4 * cg .. 4 * cg + 3 of the chunk
   const int rs = lane >> 3, cg = lane & 7;
@@ -140,7 +189,24 @@ __device__ void epilogue_tile(const GemmDesc& d, int tm, int tn, uint32_t tacc, 
   for (int it = 0; it < 8; ++it) rowacc[it] = 0.f;
   float tsum = 0.f, dsum = 0.f;
 
+  // The column pass's second input (aux, or dot_aux in SYRK mode): a chunk's loads are all issued before use.
+  const float* pre_src = syrk ? s_dot_aux : s_aux;
+  const long long pre_ld = syrk ? s_ld_dot : s_ld_aux;
+  const bool pre_vec = syrk ? vdot : vaux;
+  auto load_pre = [&](int cc, float4* out) {
+    const long long gb = n0 + cc + 4 * cg;
+    const int wn = (bn - cc) >= 32 ? 32 : 16;
+    const int nv = (4 * cg < wn) ? (int)max(0LL, min(4LL, (long long)s_N - gb)) : 0;
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const long long gr = row0 + rs + 4 * it;
+      out[it] = (gr < s_M && nv > 0) ? ld4(pre_src + gr * pre_ld + gb, nv, pre_vec && nv == 4)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
   for (int c0 = 0; c0 < bn; c0 += 32) {
+    float4 pv[8];
+    if (pre_src) load_pre(c0, pv);
     float v[32];
     const int w = (bn - c0) >= 32 ? 32 : 16;
     if (w == 32) {
@@ -158,35 +224,26 @@ __device__ void epilogue_tile(const GemmDesc& d, int tm, int tn, uint32_t tacc, 
 
     // ---- column pass ----
     const long long gcb = n0 + c0 + 4 * cg;
-    const int ncv = (4 * cg < w) ? (int)max(0LL, min(4LL, (long long)s.N - gcb)) : 0;
+    const int ncv = (4 * cg < w) ? (int)max(0LL, min(4LL, (long long)s_N - gcb)) : 0;
     float csc[4] = {1.f, 1.f, 1.f, 1.f};
     if (has_cs)
 #pragma unroll
       for (int i = 0; i < 4; ++i) csc[i] = (i < ncv) ? cs[c0 + 4 * cg + i] : 1.f;
     float csq[4] = {0.f, 0.f, 0.f, 0.f};
-    float4 av[8];
-    if (s.aux) {  // issue every aux load of the chunk before using any
-#pragma unroll
-      for (int it = 0; it < 8; ++it) {
-        const long long gr = row0 + rs + 4 * it;
-        av[it] = (gr < s.M && ncv > 0) ? ld4(s.aux + gr * s.ld_aux + gcb, ncv, vaux && ncv == 4)
-                                       : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-    }
 #pragma unroll
     for (int it = 0; it < 8; ++it) {
       const int r = rs + 4 * it;
       const long long gr = row0 + r;
-      const bool rok = gr < s.M;
+      const bool rok = gr < s_M;
       const float4 sv = *reinterpret_cast<const float4*>(stage + r * STG + 4 * cg);
       float x[4] = {sv.x, sv.y, sv.z, sv.w};
-      if (s.aux) {
-        x[0] += beta * av[it].x;
-        x[1] += beta * av[it].y;
-        x[2] += beta * av[it].z;
-        x[3] += beta * av[it].w;
+      if (s_aux) {
+        x[0] += beta * pv[it].x;
+        x[1] += beta * pv[it].y;
+        x[2] += beta * pv[it].z;
+        x[3] += beta * pv[it].w;
       }
-      const float rsc = (s.row_scale && rok) ? s.row_scale[gr] : 1.f;
+      const float rsc = (s_row_scale && rok) ? s_row_scale[gr] : 1.f;
       float rpart = 0.f;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -203,40 +260,49 @@ __device__ void epilogue_tile(const GemmDesc& d, int tm, int tn, uint32_t tacc, 
           const long long gc = gcb + i;
           if (gc >= gr) rpart += x2;
           if (gc > gr) csq[i] += x2;  // mirrored element (gc, gr) belongs to row gc
-          if (ok && gc == gr && s.diag_out) s.diag_out[gr] = xi;
+          if (ok && gc == gr && s_diag_out) s_diag_out[gr] = xi;
         }
       }
       tsum += rpart;
       rowacc[it] += rpart;
       if (rok && ncv > 0) {
         if (!syrk) {
-          if (s.out_f32) st4f(s.out_f32 + gr * s.ld_f32 + gcb, x, ncv, vf32 && ncv == 4);
-          if (out_hi) st4b(out_hi + gr * s.ld_b + gcb, out_lo ? out_lo + gr * s.ld_b + gcb : nullptr, x, ncv,
+          if (s_out_f32) st4f(s_out_f32 + gr * s_ld_f32 + gcb, x, ncv, vf32 && ncv == 4);
+          if (out_hi) st4b(out_hi + gr * s_ld_b + gcb, out_lo ? out_lo + gr * s_ld_b + gcb : nullptr, x, ncv,
                            vb16 && ncv == 4);
         } else {
           const int first = (int)max(0LL, min(4LL, gr - gcb));  // elements i >= first have gc >= gr
           if (first < ncv) {
             const bool full = first == 0 && ncv == 4;
-            if (s.out_f32) {
-              if (full) st4f(s.out_f32 + gr * s.ld_f32 + gcb, x, 4, vf32);
-              else for (int i = first; i < ncv; ++i) s.out_f32[gr * s.ld_f32 + gcb + i] = x[i];
+            if (s_out_f32) {
+              if (full) {
+                st4f(s_out_f32 + gr * s_ld_f32 + gcb, x, 4, vf32);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                  if (i >= first && i < ncv) s_out_f32[gr * s_ld_f32 + gcb + i] = x[i];
+              }
             }
             if (out_hi) {
               if (full) {
-                st4b(out_hi + gr * s.ld_b + gcb, out_lo ? out_lo + gr * s.ld_b + gcb : nullptr, x, 4, vb16);
+                st4b(out_hi + gr * s_ld_b + gcb, out_lo ? out_lo + gr * s_ld_b + gcb : nullptr, x, 4, vb16);
               } else {
-                for (int i = first; i < ncv; ++i) {
-                  __nv_bfloat16 h, l;
-                  split_bf16(x[i], h, l);
-                  out_hi[gr * s.ld_b + gcb + i] = h;
-                  if (out_lo) out_lo[gr * s.ld_b + gcb + i] = l;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  if (i >= first && i < ncv) {
+                    __nv_bfloat16 h, l;
+                    split_bf16(x[i], h, l);
+                    out_hi[gr * s_ld_b + gcb + i] = h;
+                    if (out_lo) out_lo[gr * s_ld_b + gcb + i] = l;
+                  }
                 }
               }
             }
-            if (s.dot_aux) {
-              const float4 dv = ld4(s.dot_aux + gr * s.ld_dot + gcb, ncv, vdot && ncv == 4);
-              const float dd[4] = {dv.x, dv.y, dv.z, dv.w};
-              for (int i = first; i < ncv; ++i) dsum += x[i] * dd[i];
+            if (s_dot_aux) {
+              const float dd[4] = {pv[it].x, pv[it].y, pv[it].z, pv[it].w};
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                if (i >= first && i < ncv) dsum += x[i] * dd[i];
             }
           }
         }
@@ -261,36 +327,47 @@ __device__ void epilogue_tile(const GemmDesc& d, int tm, int tn, uint32_t tacc, 
     if (tpass) {
       const int cs_ = lane >> 3, rg = lane & 7;
       const long long gr0 = row0 + 4 * rg;
-      const int nrv = (int)max(0LL, min(4LL, (long long)s.M - gr0));
-      __nv_bfloat16* ht = (__nv_bfloat16*)s.out_hi_t;
-      __nv_bfloat16* lt = (__nv_bfloat16*)s.out_lo_t;
-      const bool vt = ht && (s.ld_bt % 4 == 0) && ((reinterpret_cast<uintptr_t>(ht) & 7) == 0) &&
+      const int nrv = (int)max(0LL, min(4LL, (long long)s_M - gr0));
+      __nv_bfloat16* ht = (__nv_bfloat16*)s_out_hi_t;
+      __nv_bfloat16* lt = (__nv_bfloat16*)s_out_lo_t;
+      const bool vt = ht && (s_ld_bt % 4 == 0) && ((reinterpret_cast<uintptr_t>(ht) & 7) == 0) &&
                       (!lt || (reinterpret_cast<uintptr_t>(lt) & 7) == 0);
+      float4 md[8];  // mirrored trace operand dot_aux[gc][gr0 ..], all issued before use
+      if (syrk && s_dot_aux) {
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          const int c = 4 * it + cs_;
+          const long long gc = n0 + c0 + c;
+          const int lim = (c < w && gc < s_N) ? (int)max(0LL, min((long long)nrv, gc - gr0)) : 0;
+          md[it] = lim > 0 ? ld4(s_dot_aux + gc * s_ld_dot + gr0, lim, vdot && lim == 4)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
 #pragma unroll
       for (int it = 0; it < 8; ++it) {
         const int c = 4 * it + cs_;
         const long long gc = n0 + c0 + c;
-        if (c >= w || gc >= s.N || nrv == 0) continue;
+        if (c >= w || gc >= s_N || nrv == 0) continue;
         float x[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) x[i] = stage[(4 * rg + i) * STG + c];
         if (!syrk) {
-          st4b(ht + gc * s.ld_bt + gr0, lt ? lt + gc * s.ld_bt + gr0 : nullptr, x, nrv, vt && nrv == 4);
+          st4b(ht + gc * s_ld_bt + gr0, lt ? lt + gc * s_ld_bt + gr0 : nullptr, x, nrv, vt && nrv == 4);
         } else {
           // mirrors (gc, gr) of the elements with gc > gr: rows gr0 + i < gc
           const int lim = (int)max(0LL, min((long long)nrv, gc - gr0));
           if (lim > 0) {
             const bool full = lim == 4;
-            if (s.out_f32) {
-              if (full) st4f(s.out_f32 + gc * s.ld_f32 + gr0, x, 4, vf32);
-              else for (int i = 0; i < lim; ++i) s.out_f32[gc * s.ld_f32 + gr0 + i] = x[i];
+            if (s_out_f32) {
+              st4f(s_out_f32 + gc * s_ld_f32 + gr0, x, lim, vf32 && full);
             }
-            if (out_hi) st4b(out_hi + gc * s.ld_b + gr0, out_lo ? out_lo + gc * s.ld_b + gr0 : nullptr, x, lim,
+            if (out_hi) st4b(out_hi + gc * s_ld_b + gr0, out_lo ? out_lo + gc * s_ld_b + gr0 : nullptr, x, lim,
                              vb16 && full);
-            if (s.dot_aux) {
-              const float4 dv = ld4(s.dot_aux + gc * s.ld_dot + gr0, lim, vdot && full);
-              const float dd[4] = {dv.x, dv.y, dv.z, dv.w};
-              for (int i = 0; i < lim; ++i) dsum += x[i] * dd[i];
+            if (s_dot_aux) {
+              const float dd[4] = {md[it].x, md[it].y, md[it].z, md[it].w};
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                if (i < lim) dsum += x[i] * dd[i];
             }
           }
         }
@@ -309,7 +386,7 @@ __device__ void epilogue_tile(const GemmDesc& d, int tm, int tn, uint32_t tacc, 
     t += __shfl_xor_sync(0xffffffffu, t, 4);
     rowacc[it] = t;
   }
-  if (s.part_tile || s.part_dot) {
+  if (s_part_tile || s_part_dot) {
     const float t1 = warp_sum(tsum), t2 = warp_sum(dsum);
     if (lane == 0) {
       misc[q] = t1;
@@ -317,31 +394,242 @@ __device__ void epilogue_tile(const GemmDesc& d, int tm, int tn, uint32_t tacc, 
     }
   }
   named_sync(1, 128);
-  const long long tile_lin = (long long)tm * d.tiles_n + tn;
+  const long long tile_lin = (long long)tm * d_tiles_n + tn;
   if (et == 0) {
-    if (s.part_tile) s.part_tile[tile_lin] = ((misc[0] + misc[1]) + misc[2]) + misc[3];
-    if (s.part_dot) s.part_dot[tile_lin] = ((misc[4] + misc[5]) + misc[6]) + misc[7];
+    if (s_part_tile) s_part_tile[tile_lin] = ((misc[0] + misc[1]) + misc[2]) + misc[3];
+    if (s_part_dot) s_part_dot[tile_lin] = ((misc[4] + misc[5]) + misc[6]) + misc[7];
   }
-  if (s.part_row && cg == 0) {  // direct share: slot tn
+  if (s_part_row && cg == 0) {  // direct share: slot tn
 #pragma unroll
     for (int it = 0; it < 8; ++it) {
       const long long gr = row0 + rs + 4 * it;
-      if (gr < s.M) s.part_row[(long long)tn * s.M + gr] = rowacc[it];
+      if (gr < s_M) s_part_row[(long long)tn * s_M + gr] = rowacc[it];
     }
   }
   if (need_col) {
     for (int c = et; c < bn; c += 128) {
       const long long gcc = n0 + c;
-      if (gcc >= s.N) continue;
+      if (gcc >= s_N) continue;
       const float t = ((red[c] + red[BNMAX + c]) + red[2 * BNMAX + c]) + red[3 * BNMAX + c];
       if (!syrk) {
-        s.part_col[(long long)tm * s.N + gcc] = t;
+        s_part_col[(long long)tm * s_N + gcc] = t;
       } else {  // mirrored share of row gcc: slot tiles_n + tm
-        s.part_row[((long long)d.tiles_n + tm) * s.M + gcc] = t;
+        s_part_row[((long long)d_tiles_n + tm) * s_M + gcc] = t;
       }
     }
   }
   named_sync(1, 128);  // red/cs/misc are reused by the next tile
+}
+
+// ---- fast epilogue for interior tiles -------------------------------------------------------------------------------
+// Interior tiles (all 128 rows and bn columns inside the matrix; for SYRK, tiles strictly above the diagonal) of
+// problems whose pointers and leading dimensions allow vector accesses take a specialised path per epilogue kind:
+// no per-element masks, no tail handling, one instruction stream per kind. Same lane mappings, staging and fixed
+// reduction order as epilogue_tile.
+enum : int { EPI_GENERIC = 0, EPI_AUX = 1, EPI_NLB = 2, EPI_PLAIN = 3, EPI_SYRK = 4 };
+
+template <int KIND, int BNMAX>
+__device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn, uint32_t tacc, int q, int lane, float* red,
+                              float* cs, float* misc, float* stage) {
+  const PsgdGemmSpec& sd = d.s;
+  const long long s_M = sd.M, s_N = sd.N;
+  const int bn = sd.bn;
+  const float* __restrict__ s_aux = sd.aux;
+  const long long s_ld_aux = sd.ld_aux;
+  const float* __restrict__ s_row_scale = sd.row_scale;
+  float* __restrict__ s_out_f32 = sd.out_f32;
+  const long long s_ld_f32 = sd.ld_f32;
+  __nv_bfloat16* out_hi = (__nv_bfloat16*)sd.out_hi;
+  __nv_bfloat16* out_lo = (__nv_bfloat16*)sd.out_lo;
+  const long long s_ld_b = sd.ld_b;
+  __nv_bfloat16* ht = (__nv_bfloat16*)sd.out_hi_t;
+  __nv_bfloat16* lt = (__nv_bfloat16*)sd.out_lo_t;
+  const long long s_ld_bt = sd.ld_bt;
+  float* __restrict__ s_part_tile = sd.part_tile;
+  float* __restrict__ s_part_col = sd.part_col;
+  float* __restrict__ s_part_row = sd.part_row;
+  const float* __restrict__ s_dot = sd.dot_aux;
+  const long long s_ld_dot = sd.ld_dot;
+  float* __restrict__ s_part_dot = sd.part_dot;
+  const int d_tiles_n = d.tiles_n;
+  const long long m0 = (long long)tm * BM, n0 = (long long)tn * bn;
+  const long long row0 = m0 + q * 32;
+  const int et = q * 32 + lane;
+  const float alpha = sd.alpha * (sd.alpha_ptr ? __ldg(sd.alpha_ptr) : 1.f);
+  const float beta = sd.beta * (sd.beta_ptr ? __ldg(sd.beta_ptr) : 1.f);
+  float inv_nf = 1.f;
+  if (KIND == EPI_NLB) {  // column scales of the subspace products, in the reference's division order
+    inv_nf = 1.f / *sd.cs_nf;
+    for (int c = et; c < bn; c += 128) {
+      float v = 1.f;
+      if (sd.cs_mode == 2) {
+        float acc = 0.f;
+        for (int t = 0; t < sd.cs_T; ++t) acc += sd.cs_part[(long long)t * s_N + n0 + c];
+        v = 1.f / (sqrtf(acc) + FLT_MIN);
+      }
+      cs[c] = v;
+    }
+  }
+  named_sync(1, 128);
+
+  const int rs = lane >> 3, cg = lane & 7;     // column pass: rows rs + 4 it, columns 4 cg .. 4 cg + 3
+  const int cs_ = lane >> 3, rg = lane & 7;    // transposed pass: column 4 it + cs_, rows 4 rg .. 4 rg + 3
+  float rowacc[8];
+#pragma unroll
+  for (int it = 0; it < 8; ++it) rowacc[it] = 0.f;
+  float tsum = 0.f, dsum = 0.f;
+  const float* pre_src = KIND == EPI_AUX ? s_aux : (KIND == EPI_SYRK ? s_dot : nullptr);
+  const long long pre_ld = KIND == EPI_AUX ? s_ld_aux : s_ld_dot;
+  for (int c0 = 0; c0 < bn; c0 += 32) {
+    float4 pv[8];  // the chunk's aux / trace operand, issued before the TMEM load so their latencies overlap
+    if (pre_src) {
+#pragma unroll
+      for (int it = 0; it < 8; ++it)
+        pv[it] = *reinterpret_cast<const float4*>(pre_src + (row0 + rs + 4 * it) * pre_ld + n0 + c0 + 4 * cg);
+    }
+    float v[32];
+    tmem_ld32(tacc + (uint32_t)c0, v);
+#pragma unroll
+    for (int j = 0; j < 32; j += 4)
+      *reinterpret_cast<float4*>(stage + lane * STG + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    __syncwarp();
+    const long long colb = n0 + c0 + 4 * cg;
+    float csc[4] = {1.f, 1.f, 1.f, 1.f};
+    if (KIND == EPI_NLB) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) csc[i] = cs[c0 + 4 * cg + i];
+    }
+    float csq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int r = rs + 4 * it;
+      const long long row = row0 + r;
+      const float4 sv = *reinterpret_cast<const float4*>(stage + r * STG + 4 * cg);
+      float x[4] = {sv.x * alpha, sv.y * alpha, sv.z * alpha, sv.w * alpha};
+      if (KIND == EPI_AUX) {
+        x[0] += beta * pv[it].x;
+        x[1] += beta * pv[it].y;
+        x[2] += beta * pv[it].z;
+        x[3] += beta * pv[it].w;
+        *reinterpret_cast<float4*>(s_out_f32 + row * s_ld_f32 + colb) = make_float4(x[0], x[1], x[2], x[3]);
+      } else if (KIND == EPI_NLB) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          x[i] = (x[i] * csc[i]) * inv_nf;
+          csq[i] += x[i] * x[i];
+        }
+      } else if (KIND == EPI_PLAIN) {
+        if (s_row_scale) {
+          const float rsc = s_row_scale[row];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) x[i] *= rsc;
+        }
+        float rp = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float x2 = x[i] * x[i];
+          rp += x2;
+          csq[i] += x2;
+        }
+        tsum += rp;
+        rowacc[it] += rp;
+        if (s_out_f32)
+          *reinterpret_cast<float4*>(s_out_f32 + row * s_ld_f32 + colb) = make_float4(x[0], x[1], x[2], x[3]);
+        if (out_hi) st4b(out_hi + row * s_ld_b + colb, out_lo ? out_lo + row * s_ld_b + colb : nullptr, x, 4, true);
+      } else {  // EPI_SYRK, strictly upper tile: every element is direct and has a mirror
+        float rp = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float x2 = x[i] * x[i];
+          rp += x2;
+          csq[i] += x2;
+        }
+        rowacc[it] += rp;
+        if (s_out_f32)
+          *reinterpret_cast<float4*>(s_out_f32 + row * s_ld_f32 + colb) = make_float4(x[0], x[1], x[2], x[3]);
+        if (out_hi) st4b(out_hi + row * s_ld_b + colb, out_lo ? out_lo + row * s_ld_b + colb : nullptr, x, 4, true);
+        if (s_dot) dsum += x[0] * pv[it].x + x[1] * pv[it].y + x[2] * pv[it].z + x[3] * pv[it].w;
+      }
+      *reinterpret_cast<float4*>(stage + r * STG + 4 * cg) = make_float4(x[0], x[1], x[2], x[3]);
+    }
+    if ((KIND == EPI_NLB || KIND == EPI_PLAIN) ? (s_part_col != nullptr) : (KIND == EPI_SYRK && s_part_row)) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float t = csq[i];
+        t += __shfl_xor_sync(0xffffffffu, t, 8);
+        t += __shfl_xor_sync(0xffffffffu, t, 16);
+        csq[i] = t;
+      }
+      if (rs == 0)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) red[q * BNMAX + c0 + 4 * cg + i] = csq[i];
+    }
+    __syncwarp();
+    // transposed pass
+    __nv_bfloat16* th = KIND == EPI_SYRK ? out_hi : ht;
+    __nv_bfloat16* tl = KIND == EPI_SYRK ? out_lo : lt;
+    const long long tld = KIND == EPI_SYRK ? s_ld_b : s_ld_bt;
+    if (th || (KIND == EPI_SYRK && (s_out_f32 || s_dot))) {
+      const long long r0g = row0 + 4 * rg;
+      float4 md[8];
+      if (KIND == EPI_SYRK && s_dot) {
+#pragma unroll
+        for (int it = 0; it < 8; ++it)
+          md[it] = *reinterpret_cast<const float4*>(s_dot + (n0 + c0 + 4 * it + cs_) * s_ld_dot + r0g);
+      }
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int c = 4 * it + cs_;
+        const long long col = n0 + c0 + c;
+        float x[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) x[i] = stage[(4 * rg + i) * STG + c];
+        if (th) st4b(th + col * tld + r0g, tl ? tl + col * tld + r0g : nullptr, x, 4, true);
+        if (KIND == EPI_SYRK) {
+          if (s_out_f32)
+            *reinterpret_cast<float4*>(s_out_f32 + col * s_ld_f32 + r0g) = make_float4(x[0], x[1], x[2], x[3]);
+          if (s_dot) dsum += x[0] * md[it].x + x[1] * md[it].y + x[2] * md[it].z + x[3] * md[it].w;
+        }
+      }
+    }
+    __syncwarp();
+  }
+
+  // ---- reductions (fixed order, as epilogue_tile) ----
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    float t = rowacc[it];
+    t += __shfl_xor_sync(0xffffffffu, t, 1);
+    t += __shfl_xor_sync(0xffffffffu, t, 2);
+    t += __shfl_xor_sync(0xffffffffu, t, 4);
+    rowacc[it] = t;
+  }
+  if (s_part_tile || s_part_dot) {
+    const float t1 = warp_sum(tsum), t2 = warp_sum(dsum);
+    if (lane == 0) {
+      misc[q] = t1;
+      misc[4 + q] = t2;
+    }
+  }
+  named_sync(1, 128);
+  const long long tile_lin = (long long)tm * d_tiles_n + tn;
+  if (et == 0) {
+    if (s_part_tile) s_part_tile[tile_lin] = ((misc[0] + misc[1]) + misc[2]) + misc[3];
+    if (s_part_dot) s_part_dot[tile_lin] = ((misc[4] + misc[5]) + misc[6]) + misc[7];
+  }
+  if ((KIND == EPI_PLAIN || KIND == EPI_SYRK) && s_part_row && cg == 0) {
+#pragma unroll
+    for (int it = 0; it < 8; ++it) s_part_row[(long long)tn * s_M + row0 + rs + 4 * it] = rowacc[it];
+  }
+  const bool col_out = (KIND == EPI_NLB || KIND == EPI_PLAIN) ? (s_part_col != nullptr) : (KIND == EPI_SYRK && s_part_row);
+  if (col_out) {
+    for (int c = et; c < bn; c += 128) {
+      const float t = ((red[c] + red[BNMAX + c]) + red[2 * BNMAX + c]) + red[3 * BNMAX + c];
+      if (KIND == EPI_SYRK) s_part_row[((long long)d_tiles_n + tm) * s_M + n0 + c] = t;
+      else s_part_col[(long long)tm * s_N + n0 + c] = t;
+    }
+  }
+  named_sync(1, 128);
 }
 
 // Tile t of a launch: from the explicit list (grouped launch) or, with no list, the t-th tile of problem 0 in
@@ -370,7 +658,7 @@ PSGD_DEVI void get_tile(const GemmDesc* descs, const uint32_t* tiles, int t, int
 }
 
 // ---- the kernel body ------------------------------------------------------------------------------------------
-template <int SPLIT, int BNMAX, int STAGES>
+template <int SPLIT, int BNMAX, int STAGES, int KIND>
 __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, const uint32_t* __restrict__ tiles,
                                           int ntiles, int* err) {
   using C = GemmCfg<SPLIT, BNMAX, STAGES>;
@@ -516,7 +804,14 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
       if (!all_ok) break;
       tc_fence_after();
       const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BNMAX;
-      epilogue_tile<BNMAX>(d, tm, tn, tacc, q, lane, red, cs, misc, stage_all + q * 32 * STG);
+      float* stg = stage_all + q * 32 * STG;
+      const long long m0 = (long long)tm * BM, n0 = (long long)tn * d.s.bn;
+      const bool interior = m0 + BM <= d.s.M && n0 + d.s.bn <= d.s.N;
+      // the launch's kind (template) picks the one fast path compiled into this kernel; problems of another
+      // kind, edge tiles and SYRK tiles on the diagonal take the generic epilogue
+      const bool fast = KIND != EPI_GENERIC && d.fast == KIND && interior && (KIND != EPI_SYRK || n0 >= m0 + BM);
+      if (fast) epilogue_fast<KIND, BNMAX>(d, tm, tn, tacc, q, lane, red, cs, misc, stg);
+      else epilogue_tile<BNMAX>(d, tm, tn, tacc, q, lane, red, cs, misc, stg);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -533,18 +828,18 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
   if (threadIdx.x == 0 && *abort) atomicOr(err, ERR_TIMEOUT_FULL);
 }
 
-template <int SPLIT, int BNMAX, int STAGES>
+template <int SPLIT, int BNMAX, int STAGES, int KIND>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_group_kernel(const GemmDesc* __restrict__ descs, const uint32_t* __restrict__ tiles, int ntiles, int* err) {
-  gemm_body<SPLIT, BNMAX, STAGES>(descs, tiles, ntiles, err);
+  gemm_body<SPLIT, BNMAX, STAGES, KIND>(descs, tiles, ntiles, err);
 }
 
 // Single problem: the descriptor is a __grid_constant__ parameter and the tile list is implicit.
-template <int SPLIT, int BNMAX, int STAGES>
+template <int SPLIT, int BNMAX, int STAGES, int KIND>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_single_kernel(const __grid_constant__ GemmDesc desc, const uint32_t* __restrict__ tiles, int ntiles,
                        int* err) {
-  gemm_body<SPLIT, BNMAX, STAGES>(&desc, tiles, ntiles, err);
+  gemm_body<SPLIT, BNMAX, STAGES, KIND>(&desc, tiles, ntiles, err);
 }
 
 // ---- host side --------------------------------------------------------------------------------------------------
@@ -596,6 +891,30 @@ static int check_spec(const PsgdGemmSpec& s, int split) {
   return PSGD_OK;
 }
 
+static bool al(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
+
+// The fast epilogue kind a problem qualifies for: vector-aligned pointers and leading dimensions, and only the
+// epilogue terms that kind implements (every other problem, and every edge tile, uses the generic epilogue).
+static int fast_kind(const PsgdGemmSpec& s) {
+  const bool f32_ok = !s.out_f32 || (al(s.out_f32, 16) && s.ld_f32 % 4 == 0);
+  const bool b_ok = !s.out_hi || (al(s.out_hi, 8) && (!s.out_lo || al(s.out_lo, 8)) && s.ld_b % 4 == 0);
+  const bool t_ok = !s.out_hi_t || (al(s.out_hi_t, 8) && (!s.out_lo_t || al(s.out_lo_t, 8)) && s.ld_bt % 4 == 0);
+  const bool aux_ok = !s.aux || (al(s.aux, 16) && s.ld_aux % 4 == 0);
+  const bool dot_ok = !s.dot_aux || (al(s.dot_aux, 16) && s.ld_dot % 4 == 0);
+  // the fast epilogue walks whole 32-column chunks: narrower tiles (bn = 16) would run past the output
+  if (s.bn % 32 != 0) return EPI_GENERIC;
+  if (!(f32_ok && b_ok && t_ok && aux_ok && dot_ok) || s.col_scale) return EPI_GENERIC;
+  if (s.mode == PSGD_GEMM_SYRK) return s.row_scale || s.aux || s.cs_mode || s.out_hi_t ? EPI_GENERIC : EPI_SYRK;
+  if (s.aux)
+    return (s.out_f32 && s.out_hi_t && !s.out_hi && !s.row_scale && !s.cs_mode && !s.part_tile && !s.part_col &&
+            !s.part_row && !s.dot_aux) ? EPI_AUX : EPI_GENERIC;
+  if (s.cs_mode)
+    return (!s.out_f32 && !s.out_hi && !s.row_scale && !s.part_tile && !s.part_row && !s.dot_aux) ? EPI_NLB
+                                                                                                  : EPI_GENERIC;
+  if (s.dot_aux || s.diag_out) return EPI_GENERIC;
+  return EPI_PLAIN;
+}
+
 static int fill_desc(GemmDesc* d, const PsgdGemmSpec& s, int split) {
   int rc = check_spec(s, split);
   if (rc) return rc;
@@ -603,6 +922,7 @@ static int fill_desc(GemmDesc* d, const PsgdGemmSpec& s, int split) {
   d->s = s;
   d->tiles_m = (s.M + BM - 1) / BM;
   d->tiles_n = (s.N + s.bn - 1) / s.bn;
+  d->fast = fast_kind(s);
   if ((rc = encode_bf16(&d->ta[0], s.a_hi, s.M, s.K, s.lda, BM))) return rc;
   if ((rc = encode_bf16(&d->tb[0], s.b_hi, s.N, s.K, s.ldb, s.bn))) return rc;
   if (split != 1) {
@@ -659,24 +979,47 @@ static bool smem_attr_once(const void* fn, int bytes) {
   return true;
 }
 
-template <int SPLIT, int BNMAX, int STAGES>
+template <int SPLIT, int BNMAX, int STAGES, int KIND>
 static int launch_group(const GemmDesc* descs, const uint32_t* tiles, int ntiles, int* err, cudaStream_t st) {
   using C = GemmCfg<SPLIT, BNMAX, STAGES>;
-  auto k = gemm_group_kernel<SPLIT, BNMAX, STAGES>;
+  auto k = gemm_group_kernel<SPLIT, BNMAX, STAGES, KIND>;
   if (!smem_attr_once(reinterpret_cast<const void*>(k), C::SMEM_BYTES)) return PSGD_ELAUNCH;
   const int grid = ntiles < num_sms() ? ntiles : num_sms();
   k<<<grid, GEMM_THREADS, C::SMEM_BYTES, st>>>(descs, tiles, ntiles, err);
   return cudaGetLastError() == cudaSuccess ? PSGD_OK : PSGD_ELAUNCH;
 }
 
-template <int SPLIT, int BNMAX, int STAGES>
+template <int SPLIT, int BNMAX, int STAGES, int KIND>
 static int launch_single(const GemmDesc& desc, const uint32_t* tiles, int ntiles, int* err, cudaStream_t st) {
   using C = GemmCfg<SPLIT, BNMAX, STAGES>;
-  auto k = gemm_single_kernel<SPLIT, BNMAX, STAGES>;
+  auto k = gemm_single_kernel<SPLIT, BNMAX, STAGES, KIND>;
   if (!smem_attr_once(reinterpret_cast<const void*>(k), C::SMEM_BYTES)) return PSGD_ELAUNCH;
   const int grid = ntiles < num_sms() ? ntiles : num_sms();
   k<<<grid, GEMM_THREADS, C::SMEM_BYTES, st>>>(desc, tiles, ntiles, err);
   return cudaGetLastError() == cudaSuccess ? PSGD_OK : PSGD_ELAUNCH;
+}
+
+template <int SPLIT, int BNMAX, int STAGES>
+static int launch_group_kind(const GemmDesc* d, const uint32_t* tiles, int ntiles, int kind, int* err,
+                             cudaStream_t st) {
+  switch (kind) {
+    case EPI_AUX: return launch_group<SPLIT, BNMAX, STAGES, EPI_AUX>(d, tiles, ntiles, err, st);
+    case EPI_NLB: return launch_group<SPLIT, BNMAX, STAGES, EPI_NLB>(d, tiles, ntiles, err, st);
+    case EPI_PLAIN: return launch_group<SPLIT, BNMAX, STAGES, EPI_PLAIN>(d, tiles, ntiles, err, st);
+    case EPI_SYRK: return launch_group<SPLIT, BNMAX, STAGES, EPI_SYRK>(d, tiles, ntiles, err, st);
+    default: return launch_group<SPLIT, BNMAX, STAGES, EPI_GENERIC>(d, tiles, ntiles, err, st);
+  }
+}
+
+template <int SPLIT, int BNMAX, int STAGES>
+static int launch_single_kind(const GemmDesc& d, int ntiles, int* err, cudaStream_t st) {
+  switch (d.fast) {
+    case EPI_AUX: return launch_single<SPLIT, BNMAX, STAGES, EPI_AUX>(d, nullptr, ntiles, err, st);
+    case EPI_NLB: return launch_single<SPLIT, BNMAX, STAGES, EPI_NLB>(d, nullptr, ntiles, err, st);
+    case EPI_PLAIN: return launch_single<SPLIT, BNMAX, STAGES, EPI_PLAIN>(d, nullptr, ntiles, err, st);
+    case EPI_SYRK: return launch_single<SPLIT, BNMAX, STAGES, EPI_SYRK>(d, nullptr, ntiles, err, st);
+    default: return launch_single<SPLIT, BNMAX, STAGES, EPI_GENERIC>(d, nullptr, ntiles, err, st);
+  }
 }
 
 }  // namespace psgd
@@ -698,8 +1041,8 @@ extern "C" int psgd_gemm_count_tiles(const PsgdGemmSpec* specs, int nspecs) {
 }
 
 extern "C" int psgd_gemm_encode(const PsgdGemmSpec* specs, int nspecs, void* host_table, size_t table_bytes,
-                                uint32_t* host_tiles, int max_tiles, int* ntiles) {
-  if (!specs || nspecs < 1 || !host_table || !host_tiles || !ntiles) return PSGD_EINVAL;
+                                uint32_t* host_tiles, int max_tiles, int* ntiles, int* kind) {
+  if (!specs || nspecs < 1 || !host_table || !host_tiles || !ntiles || !kind) return PSGD_EINVAL;
   if (table_bytes < psgd_gemm_table_bytes(nspecs) || (reinterpret_cast<uintptr_t>(host_table) & 63)) return PSGD_ESPACE;
   if (nspecs > 65535) return PSGD_EINVAL;
   const int need = psgd_gemm_count_tiles(specs, nspecs);
@@ -715,16 +1058,23 @@ extern "C" int psgd_gemm_encode(const PsgdGemmSpec* specs, int nspecs, void* hos
   int k = 0;
   for (int i = 0; i < nspecs; ++i) append_tiles(specs[i], (uint32_t)i, host_tiles, k);
   *ntiles = k;
+  // the group's epilogue kind: the fast kind covering the most tiles (its problems take the fast path)
+  long long w[5] = {0, 0, 0, 0, 0};
+  for (int i = 0; i < nspecs; ++i) w[descs[i].fast] += spec_tiles(specs[i]);
+  int best = EPI_GENERIC;
+  for (int t = 1; t < 5; ++t)
+    if (w[t] > w[best] || (best == EPI_GENERIC && w[t] > 0)) best = t;
+  *kind = best;
   return PSGD_OK;
 }
 
-extern "C" int psgd_gemm_launch(const void* dev_table, const uint32_t* dev_tiles, int ntiles, int split, int* dev_err,
-                                cudaStream_t stream) {
-  if (!dev_table || !dev_tiles || ntiles < 0 || !dev_err) return PSGD_EINVAL;
+extern "C" int psgd_gemm_launch(const void* dev_table, const uint32_t* dev_tiles, int ntiles, int split, int kind,
+                                int* dev_err, cudaStream_t stream) {
+  if (!dev_table || !dev_tiles || ntiles < 0 || !dev_err || kind < 0 || kind > 4) return PSGD_EINVAL;
   if (ntiles == 0) return PSGD_OK;
   const GemmDesc* d = reinterpret_cast<const GemmDesc*>(dev_table);
-  if (split == 1) return launch_group<1, 256, 4>(d, dev_tiles, ntiles, dev_err, stream);
-  if (split == 3) return launch_group<3, 128, 3>(d, dev_tiles, ntiles, dev_err, stream);
+  if (split == 1) return launch_group_kind<1, 256, 4>(d, dev_tiles, ntiles, kind, dev_err, stream);
+  if (split == 3) return launch_group_kind<3, 128, 3>(d, dev_tiles, ntiles, kind, dev_err, stream);
   return PSGD_EINVAL;
 }
 
@@ -734,6 +1084,6 @@ extern "C" int psgd_gemm(const PsgdGemmSpec* spec, int split, int* dev_err, cuda
   int rc = fill_desc(&desc, *spec, split);
   if (rc) return rc;
   const int nt = spec_tiles(*spec);
-  if (split == 1) return launch_single<1, 256, 4>(desc, nullptr, nt, dev_err, stream);
-  return launch_single<3, 128, 3>(desc, nullptr, nt, dev_err, stream);
+  if (split == 1) return launch_single_kind<1, 256, 4>(desc, nt, dev_err, stream);
+  return launch_single_kind<3, 128, 3>(desc, nt, dev_err, stream);
 }

@@ -12,6 +12,7 @@ namespace psgd {
 
 constexpr int TT = 32;        // tile edge of the tiled element-wise kernels
 constexpr int TROWS = 8;      // threads per tile column (256 threads, 4 rows each)
+constexpr int PREP_ROWS = PSGD_PREP_ROWS;  // rows per work entry of the row-vector staging path
 
 PSGD_DEVI float load_g(const void* g, int bf16, long long idx) {
   return bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(g)[idx])
@@ -42,6 +43,52 @@ __global__ void __launch_bounds__(256) prep_kernel(const PsgdPrepItem* __restric
   const float damping = hyper[PSGD_HY_DAMPING];
   for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
     const PsgdPrepItem& it = items[work[2 * w]];
+    if (it.mode == PSGD_PREP_NORMAL) {  // rows PREP_ROWS * wv .. : 4-element vectors along each row
+      const long long r0 = (long long)work[2 * w + 1] * PREP_ROWS;
+      const int rows = (int)min((long long)PREP_ROWS, it.n1 - r0);
+      const bool vec = (it.n2 % 4) == 0 &&
+                       ((reinterpret_cast<uintptr_t>(it.g) & (it.g_bf16 ? 7 : 15)) == 0) &&
+                       (it.xi == nullptr || (reinterpret_cast<uintptr_t>(it.xi) & 15) == 0);
+      if (vec) {
+        const int nv = it.n2 / 4;
+        for (int k = threadIdx.x; k < rows * nv; k += blockDim.x) {
+          const long long row = r0 + k / nv, col = (long long)(k % nv) * 4;
+          const long long idx = row * it.n2 + col;
+          float x[4];
+          if (it.g_bf16) {
+            const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(it.g) + idx);
+            const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) x[i] = __bfloat162float(h[i]);
+          } else {
+            const float4 v = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(it.g) + idx);
+            x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+          }
+          if (it.xi) {
+            const float4 z = *reinterpret_cast<const float4*>(it.xi + idx);
+            const float zz[4] = {z.x, z.y, z.z, z.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) x[i] += (damping + it.eps * fabsf(x[i])) * zz[i];
+          }
+          __align__(8) __nv_bfloat16 h[4], l[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) split_bf16(x[i], h[i], l[i]);
+          const long long o = row * it.ld_out + col;
+          *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(it.out_hi) + o) = *reinterpret_cast<const uint2*>(h);
+          if (it.out_lo)
+            *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(it.out_lo) + o) = *reinterpret_cast<const uint2*>(l);
+        }
+      } else {
+        for (int k = threadIdx.x; k < rows * it.n2; k += blockDim.x) {
+          const long long row = r0 + k / it.n2, col = k % it.n2;
+          const long long idx = row * it.n2 + col;
+          float x = load_g(it.g, it.g_bf16, idx);
+          if (it.xi) x += (damping + it.eps * fabsf(x)) * it.xi[idx];
+          store_split(it.out_hi, it.out_lo, row * it.ld_out + col, x);
+        }
+      }
+      continue;
+    }
     const int ti = work[2 * w + 1] >> 16, tj = work[2 * w + 1] & 0xFFFF;
     const int i0 = ti * TT, j0 = tj * TT;
     const int j = j0 + tx;
@@ -57,13 +104,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const PsgdPrepItem* __restric
       }
       vals[u] = x;
     }
-    if (it.mode == PSGD_PREP_NORMAL) {
-#pragma unroll
-      for (int u = 0; u < TT / TROWS; ++u) {
-        const int i = i0 + ty + u * TROWS;
-        if (i < it.n1 && j < it.n2) store_split(it.out_hi, it.out_lo, (long long)i * it.ld_out + j, vals[u]);
-      }
-    } else if (it.mode == PSGD_PREP_TRANS) {
+    if (it.mode == PSGD_PREP_TRANS) {
       const float s2 = (it.p2 && j < it.n2) ? it.p2[j] : 1.f;
 #pragma unroll
       for (int u = 0; u < TT / TROWS; ++u) tile[ty + u * TROWS][tx] = vals[u] * s2;
@@ -287,71 +328,154 @@ __global__ void __launch_bounds__(FAC_THREADS) factor_kernel(const PsgdFactorIte
 }
 
 // ---- Rn = Q - Q^T ------------------------------------------------------------------------------------------------
+// One block per tile pair (ti <= tj): tiles A = Q[ti, tj] and B = Q[tj, ti] are read once (float4 when n % 4 == 0)
+// and both Rn tiles, Rn[ti, tj] = A - B^T and Rn[tj, ti] = B - A^T, are written (8-byte bf16 stores).
+PSGD_DEVI void st4_split(void* hi, void* lo, long long idx, const float* x, bool vec, int nvalid) {
+  __align__(8) __nv_bfloat16 h[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) split_bf16(x[i], h[i], l[i]);
+  __nv_bfloat16* H = reinterpret_cast<__nv_bfloat16*>(hi) + idx;
+  __nv_bfloat16* L = lo ? reinterpret_cast<__nv_bfloat16*>(lo) + idx : nullptr;
+  if (vec) {
+    *reinterpret_cast<uint2*>(H) = *reinterpret_cast<const uint2*>(h);
+    if (L) *reinterpret_cast<uint2*>(L) = *reinterpret_cast<const uint2*>(l);
+  } else {
+    for (int i = 0; i < nvalid; ++i) {
+      H[i] = h[i];
+      if (L) L[i] = l[i];
+    }
+  }
+}
+
 __global__ void __launch_bounds__(256) skew_kernel(const PsgdSkewItem* __restrict__ items,
                                                   const uint32_t* __restrict__ work, int nwork) {
-  __shared__ float tT[TT][TT + 1];
-  __shared__ float colred[TROWS][2];
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  __shared__ float sA[TT][TT + 1], sB[TT][TT + 1];
+  __shared__ float red[8][2];
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
+  const int r = t >> 3, c4 = (t & 7) * 4;  // this thread: row r, columns c4 .. c4 + 3 of a tile
   for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
     const PsgdSkewItem& it = items[work[2 * w]];
     const int ti = work[2 * w + 1] >> 16, tj = work[2 * w + 1] & 0xFFFF;
     const int n = it.n, i0 = ti * TT, j0 = tj * TT;
-    // Q^T tile: tT[c][r] = Q[j0 + c][i0 + r] loaded coalesced along r
+    const bool diag = ti == tj;
+    const bool vec = (n % 4) == 0;
+    // load A (rows i0.., cols j0..) and B (rows j0.., cols i0..)
+    {
+      const int ia = i0 + r, ja = j0 + c4, ib = j0 + r, jb = i0 + c4;
+      float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
+      if (ia < n) {
+        if (vec && ja + 3 < n) {
+          const float4 v = *reinterpret_cast<const float4*>(it.q + (long long)ia * n + ja);
+          a[0] = v.x; a[1] = v.y; a[2] = v.z; a[3] = v.w;
+        } else {
+          for (int k = 0; k < 4; ++k) if (ja + k < n) a[k] = it.q[(long long)ia * n + ja + k];
+        }
+      }
+      if (!diag && ib < n) {
+        if (vec && jb + 3 < n) {
+          const float4 v = *reinterpret_cast<const float4*>(it.q + (long long)ib * n + jb);
+          b[0] = v.x; b[1] = v.y; b[2] = v.z; b[3] = v.w;
+        } else {
+          for (int k = 0; k < 4; ++k) if (jb + k < n) b[k] = it.q[(long long)ib * n + jb + k];
+        }
+      }
 #pragma unroll
-    for (int u = 0; u < TT / TROWS; ++u) {
-      const int c = ty + u * TROWS, gi = j0 + c, gj = i0 + tx;
-      tT[c][tx] = (gi < n && gj < n) ? it.q[(long long)gi * n + gj] : 0.f;
+      for (int k = 0; k < 4; ++k) {
+        sA[r][c4 + k] = a[k];
+        sB[r][c4 + k] = b[k];
+      }
     }
     __syncthreads();
-    float mx = 0.f, dsum = 0.f;
-    const int j = j0 + tx;
+    if (diag) {
 #pragma unroll
-    for (int u = 0; u < TT / TROWS; ++u) {
-      const int r = ty + u * TROWS, i = i0 + r;
-      float v = 0.f, q = 0.f;
-      if (i < n && j < n) {
-        q = it.q[(long long)i * n + j];
-        v = q - tT[tx][r];  // Q[i][j] - Q[j][i]
-        store_split(it.r_hi, it.r_lo, (long long)i * it.ldr + j, v);
+      for (int k = 0; k < 4; ++k) sB[r][c4 + k] = sA[r][c4 + k];
+      __syncthreads();
+    }
+    float mx = 0.f, dsum = 0.f;
+    const int tiles = (n + TT - 1) / TT;
+    for (int half = 0; half < (diag ? 1 : 2); ++half) {
+      // half 0: Rn[ti, tj] rows i0 + r = A[r][c] - B[c][r]; half 1: Rn[tj, ti] rows j0 + r = B[r][c] - A[c][r]
+      const float(*X)[TT + 1] = half == 0 ? sA : sB;
+      const float(*Y)[TT + 1] = half == 0 ? sB : sA;
+      const int gi = (half == 0 ? i0 : j0) + r, gj0 = (half == 0 ? j0 : i0) + c4;
+      float v[4], rs = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const bool ok = gi < n && gj0 + k < n;
+        v[k] = ok ? X[r][c4 + k] - Y[c4 + k][r] : 0.f;
+        rs += v[k] * v[k];
+        mx = fmaxf(mx, fabsf(v[k]));
+        dsum += v[k] * X[r][c4 + k];
       }
-      const float rs = warp_sum(v * v);
-      if (tx == 0 && i < n) it.part_row[(long long)tj * n + i] = rs;
-      mx = fmaxf(mx, fabsf(v));
-      dsum += v * q;
+      if (gi < n) {
+        const int nv = max(0, min(4, n - gj0));
+        if (nv > 0) st4_split(it.r_hi, it.r_lo, (long long)gi * it.ldr + gj0, v, nv == 4 && (it.ldr % 4) == 0, nv);
+      }
+      rs += __shfl_xor_sync(0xffffffffu, rs, 1);
+      rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+      rs += __shfl_xor_sync(0xffffffffu, rs, 4);
+      const int slot = half == 0 ? tj : ti;
+      if ((t & 7) == 0 && gi < n) it.part_row[(long long)slot * n + gi] = rs;
     }
     mx = warp_max(mx);
     dsum = warp_sum(dsum);
-    if (tx == 0) { colred[ty][0] = mx; colred[ty][1] = dsum; }
+    if (lane == 0) { red[wid][0] = mx; red[wid][1] = dsum; }
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (t == 0) {
       float m = 0.f, d = 0.f;
-      for (int r = 0; r < TROWS; ++r) { m = fmaxf(m, colred[r][0]); d += colred[r][1]; }
-      const int tiles = (n + TT - 1) / TT;
-      it.part_max[(long long)ti * tiles + tj] = m;
+      for (int k = 0; k < 8; ++k) { m = fmaxf(m, red[k][0]); d += red[k][1]; }
+      it.part_max[(long long)ti * tiles + tj] = m;  // the pair's max and trace share, in the (ti, tj) slot
       it.part_dot[(long long)ti * tiles + tj] = d;
     }
     __syncthreads();
   }
 }
 
-// ---- M = alpha Rn + beta S ---------------------------------------------------------------------------------------
+// ---- M = a Rn / s + a^2 / 2 (S / s) / s ----------------------------------------------------------------------------
+// Rows of the padded n x ld bf16 arrays, 8 values (16 bytes) per vector; padding columns are zero and stay zero.
+// Work entries: (item, first row of a block of ROT_ROWS rows).
+constexpr int ROT_ROWS = 4;
+
+PSGD_DEVI void unpack8(const uint4& u, float* f) {
+  const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = __bfloat162float(h[i]);
+}
+
 __global__ void __launch_bounds__(256) rot_kernel(const PsgdRotItem* __restrict__ items,
                                                  const uint32_t* __restrict__ work, int nwork) {
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
     const PsgdRotItem& it = items[work[2 * w]];
-    const int ti = work[2 * w + 1] >> 16, tj = work[2 * w + 1] & 0xFFFF;
+    const int r0 = (int)work[2 * w + 1];
     const float a = *it.alpha, inv_s = *it.beta, half_a2 = 0.5f * a * a;
-    const int j = tj * TT + tx;
+    const int nvec = (int)(it.ldr / 8);
+    const int rows = min(ROT_ROWS, it.n - r0);
+    for (int k = threadIdx.x; k < rows * nvec; k += blockDim.x) {
+      const long long row = r0 + k / nvec, col = (long long)(k % nvec) * 8;
+      uint4* rh = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(it.r_hi) + row * it.ldr + col);
+      const uint4* sh = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(it.s_hi) + row * it.lds + col);
+      float rv[8], sv[8];
+      unpack8(*rh, rv);
+      unpack8(*sh, sv);
+      uint4* rl = nullptr;
+      if (it.r_lo) {
+        rl = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(it.r_lo) + row * it.ldr + col);
+        float l[8];
+        unpack8(*rl, l);
 #pragma unroll
-    for (int u = 0; u < TT / TROWS; ++u) {
-      const int i = ti * TT + ty + u * TROWS;
-      if (i < it.n && j < it.n) {
-        const float r = load_split(it.r_hi, it.r_lo, (long long)i * it.ldr + j);
-        const float s = load_split(it.s_hi, it.s_lo, (long long)i * it.lds + j);
-        // M = a Rn/s + a^2/2 (S/s)/s, with the normalised factors formed first (no overflow for tiny s)
-        store_split(it.r_hi, it.r_lo, (long long)i * it.ldr + j, a * (r * inv_s) + half_a2 * ((s * inv_s) * inv_s));
+        for (int i = 0; i < 8; ++i) rv[i] += l[i];
       }
+      if (it.s_lo) {
+        float l[8];
+        unpack8(*reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(it.s_lo) + row * it.lds + col), l);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sv[i] += l[i];
+      }
+      __align__(16) __nv_bfloat16 h[8], l[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) split_bf16(a * (rv[i] * inv_s) + half_a2 * ((sv[i] * inv_s) * inv_s), h[i], l[i]);
+      *rh = *reinterpret_cast<const uint4*>(h);
+      if (rl) *rl = *reinterpret_cast<const uint4*>(l);
     }
   }
 }
@@ -380,6 +504,41 @@ __global__ void __launch_bounds__(256) apply_kernel(const PsgdApplyItem* __restr
     const long long base = (long long)work[2 * w + 1] * PSGD_APPLY_CHUNK;
     const float sc = *it.scale;
     const long long end = min(base + (long long)PSGD_APPLY_CHUNK, it.numel);
+    const bool vec = ((reinterpret_cast<uintptr_t>(it.pg) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(it.param) & (it.param_bf16 ? 7 : 15)) == 0);
+    if (vec) {  // whole 4-element vectors (chunk bases are multiples of 4), then the tail
+      const long long vend = base + ((end - base) / 4) * 4;
+      for (long long k = base + 4 * threadIdx.x; k < vend; k += 4 * blockDim.x) {
+        const float4 g4 = *reinterpret_cast<const float4*>(it.pg + k);
+        float g[4] = {g4.x, g4.y, g4.z, g4.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) g[i] = fminf(fmaxf(g[i] * sc, -me), me);
+        if (it.param_bf16) {
+          uint2* pp = reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(it.param) + k);
+          uint2 u = *pp;
+          __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&u);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) h[i] = __float2bfloat16_rn(__bfloat162float(h[i]) - lr * g[i]);
+          *pp = u;
+        } else {
+          float4* pp = reinterpret_cast<float4*>(reinterpret_cast<float*>(it.param) + k);
+          float4 p = *pp;
+          p.x -= lr * g[0]; p.y -= lr * g[1]; p.z -= lr * g[2]; p.w -= lr * g[3];
+          *pp = p;
+        }
+      }
+      for (long long k = vend + threadIdx.x; k < end; k += blockDim.x) {
+        const float g = fminf(fmaxf(it.pg[k] * sc, -me), me);
+        if (it.param_bf16) {
+          __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(it.param);
+          p[k] = __float2bfloat16_rn(__bfloat162float(p[k]) - lr * g);
+        } else {
+          float* p = reinterpret_cast<float*>(it.param);
+          p[k] = p[k] - lr * g;
+        }
+      }
+      continue;
+    }
     for (long long k = base + threadIdx.x; k < end; k += blockDim.x) {
       const float g = fminf(fmaxf(it.pg[k] * sc, -me), me);
       if (it.param_bf16) {
@@ -390,6 +549,91 @@ __global__ void __launch_bounds__(256) apply_kernel(const PsgdApplyItem* __restr
         p[k] = p[k] - lr * g;
       }
     }
+  }
+}
+
+// ---- factor balancing (psgd_pro.py:96-105) --------------------------------------------------------------------------
+// max |q| per chunk of a factor's values, then per parameter gmean / max, then one pass that rescales Q (fp32),
+// rewrites Q^T (transposed, bf16 hi/lo) and P = Q^T Q (times c^2), or q and p = q^2 for a diagonal factor.
+__global__ void __launch_bounds__(256) absmax_kernel(const PsgdBalanceFactor* __restrict__ fs,
+                                                    const uint32_t* __restrict__ work, int nwork) {
+  __shared__ float red[8];
+  for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
+    const PsgdBalanceFactor& f = fs[work[2 * w]];
+    const long long numel = f.dense ? (long long)f.n * f.n : f.n;
+    const long long base = (long long)work[2 * w + 1] * PSGD_APPLY_CHUNK;
+    const long long end = min(base + (long long)PSGD_APPLY_CHUNK, numel);
+    float m = 0.f;
+    for (long long k = base + threadIdx.x; k < end; k += blockDim.x) m = fmaxf(m, fabsf(f.q[k]));
+    m = warp_max(m);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.f;
+      for (int i = 0; i < 8; ++i) t = fmaxf(t, red[i]);
+      f.part[work[2 * w + 1]] = t;
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void __launch_bounds__(32) balance_scale_kernel(const PsgdBalanceFactor* __restrict__ fs,
+                                                          const PsgdBalanceParam* __restrict__ ps) {
+  const PsgdBalanceParam& p = ps[blockIdx.x];
+  if (threadIdx.x != 0) return;
+  float norms[8];
+  float prod = 1.f;
+  const int nf = min(p.nf, 8);
+  for (int k = 0; k < nf; ++k) {
+    const PsgdBalanceFactor& f = fs[p.f0 + k];
+    float m = 0.f;
+    for (int i = 0; i < f.nparts; ++i) m = fmaxf(m, f.part[i]);
+    norms[k] = m;
+    prod *= m;
+  }
+  const float gmean = powf(prod, 1.f / (float)nf);
+  for (int k = 0; k < nf; ++k) *fs[p.f0 + k].scale = gmean / norms[k];
+}
+
+__global__ void __launch_bounds__(256) balance_apply_kernel(const PsgdBalanceFactor* __restrict__ fs,
+                                                           const uint32_t* __restrict__ work, int nwork) {
+  __shared__ float tile[TT][TT + 1];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
+    const PsgdBalanceFactor& f = fs[work[2 * w]];
+    const float c = *f.scale;
+    if (!f.dense) {
+      const long long base = (long long)work[2 * w + 1] * PSGD_APPLY_CHUNK;
+      const long long end = min(base + (long long)PSGD_APPLY_CHUNK, (long long)f.n);
+      for (long long k = base + threadIdx.x; k < end; k += blockDim.x) {
+        const float q = f.q[k] * c;
+        f.q[k] = q;
+        f.pdiag[k] = q * q;
+      }
+      continue;
+    }
+    const int ti = work[2 * w + 1] >> 16, tj = work[2 * w + 1] & 0xFFFF;
+    const int n = f.n, i0 = ti * TT, j0 = tj * TT;
+    const float c2 = c * c;
+#pragma unroll
+    for (int u = 0; u < TT / TROWS; ++u) {
+      const int i = i0 + ty + u * TROWS, j = j0 + tx;
+      float q = 0.f;
+      if (i < n && j < n) {
+        q = f.q[(long long)i * n + j] * c;
+        f.q[(long long)i * n + j] = q;
+        const float pv = load_split(f.p_hi, f.p_lo, (long long)i * f.ldp + j) * c2;
+        store_split(f.p_hi, f.p_lo, (long long)i * f.ldp + j, pv);
+      }
+      tile[ty + u * TROWS][tx] = q;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < TT / TROWS; ++u) {  // Q^T[j][i] = Q[i][j]
+      const int jj = j0 + ty + u * TROWS, ii = i0 + tx;
+      if (jj < n && ii < n) store_split(f.qt_hi, f.qt_lo, (long long)jj * f.ldqt + ii, tile[tx][ty + u * TROWS]);
+    }
+    __syncthreads();
   }
 }
 
@@ -454,5 +698,19 @@ extern "C" int psgd_apply(const PsgdApplyItem* items, int nitems, const uint32_t
   if (rc) return rc;
   if (nwork == 0) return PSGD_OK;
   apply_kernel<<<grid_for(nwork), 256, 0, stream>>>(items, work, nwork, hyper);
+  return launched();
+}
+
+extern "C" int psgd_balance(const PsgdBalanceFactor* factors, const PsgdBalanceParam* params, int nparams,
+                            const uint32_t* work_max, int nwork_max, const uint32_t* work_apply, int nwork_apply,
+                            int* dev_err, cudaStream_t stream) {
+  if (!factors || !params || nparams < 0 || nwork_max < 0 || nwork_apply < 0) return PSGD_EINVAL;
+  if (nparams == 0) return PSGD_OK;
+  if (nwork_max) absmax_kernel<<<grid_for(nwork_max), 256, 0, stream>>>(factors, work_max, nwork_max);
+  int rc = launched();
+  if (rc) return rc;
+  balance_scale_kernel<<<nparams, 32, 0, stream>>>(factors, params);
+  if ((rc = launched())) return rc;
+  if (nwork_apply) balance_apply_kernel<<<grid_for(nwork_apply), 256, 0, stream>>>(factors, work_apply, nwork_apply);
   return launched();
 }

@@ -87,10 +87,10 @@ class GemmGroup:
         off = (-host_table.data_ptr()) % 64
         host_table = host_table[off:off + nbytes]
         host_tiles = torch.empty(2 * max(ntiles_max, 1), dtype=torch.int32)
-        nt = ctypes.c_int(0)
+        nt, kind = ctypes.c_int(0), ctypes.c_int(0)
         check(L.psgd_gemm_encode(self.specs, len(specs), host_table.data_ptr(), nbytes, host_tiles.data_ptr(),
-                                 ntiles_max, ctypes.byref(nt)), "psgd_gemm_encode")
-        self.ntiles = nt.value
+                                 ntiles_max, ctypes.byref(nt), ctypes.byref(kind)), "psgd_gemm_encode")
+        self.ntiles, self.kind = nt.value, kind.value
         self.flops = sum((s.M * s.M * s.K) if s.mode == PSGD_GEMM_SYRK else (2 * s.M * s.N * s.K) for s in specs)
         self.table = host_table.to(device)
         self.tiles = host_tiles[:2 * max(self.ntiles, 1)].to(device)
@@ -98,4 +98,4 @@ class GemmGroup:
 
     def launch(self, err):
         check(_capi.lib().psgd_gemm_launch(self.table.data_ptr(), self.tiles.data_ptr(), self.ntiles, self.split,
-                                           ptr(err), stream_handle()), "psgd_gemm_launch")
+                                           self.kind, ptr(err), stream_handle()), "psgd_gemm_launch")

@@ -179,11 +179,12 @@ class _Plan:
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
         self.clip = torch.zeros(max(1, len(self.params)), device=device)
         # random draws: the damping noise of every parameter, then two 32 x n starts per dense factor
-        self.xi = torch.zeros(sum(p.numel for p in self.params), device=device)
+        # each parameter's slice starts on a 16-byte boundary (vector loads)
+        self.xi = torch.zeros(sum(cdiv(p.numel, 4) * 4 for p in self.params), device=device)
         off = 0
         for p in self.params:
             p.xi = self.xi[off:off + p.numel].view(p.n1, p.n2)
-            off += p.numel
+            off += cdiv(p.numel, 4) * 4
         dense = [f for f in self.factors if f.kind == "dense"]
         self.vbuf = torch.zeros(sum(2 * K_SUB * f.n for f in dense), device=device)
         off = 0
@@ -253,7 +254,10 @@ class _Plan:
                         p.apart = torch.zeros(cdiv(p.n1, TT) * cdiv(p.n2, TT), device=dev)
                         it.out_f32, it.part_tile = p.pg32.data_ptr(), p.apart.data_ptr()
                 items.append(it)
-                pairs += _tile_pairs(len(items) - 1, p.n1, p.n2)
+                if it.mode == PSGD_PREP_NORMAL:
+                    pairs += [(len(items) - 1, rb) for rb in range(cdiv(p.n1, _capi.PREP_ROWS))]
+                else:
+                    pairs += _tile_pairs(len(items) - 1, p.n1, p.n2)
         self.prep_u_dev = _upload(_capi.PrepItem, self.prep_u, dev)
         self.prep_a_dev = _upload(_capi.PrepItem, self.prep_a, dev)
         self.prep_u_work, self.prep_u_n = _work(pu, dev)
@@ -334,7 +338,7 @@ class _Plan:
             it.q, it.n, it.r_hi, it.r_lo, it.ldr = f.q.data_ptr(), f.n, K.ptr(f.R[0]), K.ptr(f.R[1]), f.R[0].stride(0)
             it.part_row, it.part_max, it.part_dot = f.r_rows.data_ptr(), f.r_max.data_ptr(), f.r_dot.data_ptr()
             sk.append(it)
-            skw += _tile_pairs(len(sk) - 1, f.n, f.n)
+            skw += [(len(sk) - 1, (ti << 16) | tj) for ti in range(f.T32) for tj in range(ti, f.T32)]
         self.skew_dev = _upload(_capi.SkewItem, sk, dev)
         self.skew_work, self.skew_n = _work(skw, dev)
         # U12..U16: norm lower bound of Rn (skew)
@@ -362,7 +366,7 @@ class _Plan:
             it.s_hi, it.s_lo, it.lds = K.ptr(f.T[0]), K.ptr(f.T[1]), f.T[0].stride(0)
             it.alpha, it.beta = self.s(f, S_AM).data_ptr(), self.s(f, S_BM).data_ptr()
             ri.append(it)
-            rw += _tile_pairs(len(ri) - 1, f.n, f.n)
+            rw += [(len(ri) - 1, r0) for r0 in range(0, f.n, 4)]
         self.rot_dev = _upload(_capi.RotItem, ri, dev)
         self.rot_work, self.rot_n = _work(rw, dev)
         # U20: Q <- Q - M Q
@@ -401,6 +405,32 @@ class _Plan:
             aw += [(k, c) for c in range(cdiv(p.numel, APPLY_CHUNK))]
         self.apply_dev, self.apply_n = _upload(_capi.ApplyItem, ai, dev), len(ai)
         self.apply_work, self.apply_nw = _work(aw, dev)
+        # factor balancing of one parameter (launched only when its coin fires)
+        self.balance = {}
+        for k, p in enumerate(P):
+            if len(p.factors) < 2:
+                continue
+            fl, wm, wa = [], [], []
+            for f in p.factors:
+                numel = f.n * f.n if f.kind == "dense" else f.n
+                nparts = cdiv(numel, APPLY_CHUNK)
+                f.bal = torch.zeros(nparts + 1, device=dev)  # per-chunk max |q|, then the multiplier
+                it = _capi.BalanceFactor()
+                it.q, it.n, it.dense = f.q.data_ptr(), f.n, int(f.kind == "dense")
+                it.part, it.nparts, it.scale = f.bal.data_ptr(), nparts, f.bal[nparts:].data_ptr()
+                if f.kind == "dense":
+                    it.qt_hi, it.qt_lo, it.ldqt = K.ptr(f.qta[0]), K.ptr(f.qta[1]), f.qta[0].stride(0)
+                    it.p_hi, it.p_lo, it.ldp = K.ptr(f.P[0]), K.ptr(f.P[1]), f.P[0].stride(0)
+                    wa += [(len(fl), (ti << 16) | tj) for ti in range(f.T32) for tj in range(f.T32)]
+                else:
+                    it.pdiag = f.p.data_ptr()
+                    wa += [(len(fl), c) for c in range(nparts)]
+                wm += [(len(fl), c) for c in range(nparts)]
+                fl.append(it)
+            wmd, nwm = _work(wm, dev)
+            wad, nwa = _work(wa, dev)
+            self.balance[k] = (_upload(_capi.BalanceFactor, fl, dev),
+                               _upload(_capi.BalanceParam, [_capi.BalanceParam(0, len(fl))], dev), wmd, nwm, wad, nwa)
 
     def _nlb_prep(self, fs, skew):
         items = []
@@ -652,19 +682,18 @@ class KronWhiten:
             self._plan.hyper.copy_(torch.tensor(h, dtype=torch.float32))
             self._hyper_host = h
 
-    def _balance(self, k):
-        """psgd_pro.py:96-105 for parameter k (rare: coin probability 0.01 per step); refreshes Q^T and P."""
-        p = self._plan.params[k]
-        if len(p.factors) < 2:
-            return
-        norms = [f.q.abs().max() for f in p.factors]
-        gmean = torch.prod(torch.stack(norms)) ** (1.0 / len(norms))
-        for f, nm in zip(p.factors, norms):
-            f.q.mul_(gmean / nm)
-            if f.kind == "dense":
-                f.refresh_operands()
-            else:
-                f.p.copy_(f.q * f.q)
+    def _balance(self, ks):
+        """psgd_pro.py:96-105 for the parameters ks whose coin fired (probability 0.01 each per step): one
+        psgd_balance call per parameter rescales its factors and their Q^T / P operand copies on the device, from
+        item arrays and work lists encoded when the plan was built."""
+        plan = self._plan
+        for k in ks:
+            b = plan.balance.get(k)
+            if b is None:  # order-1 preconditioners are left alone (psgd_pro.py:101)
+                continue
+            fdev, pdev, wmd, nwm, wad, nwa = b
+            check(_capi.lib().psgd_balance(fdev.data_ptr(), pdev.data_ptr(), 1, wmd.data_ptr(), nwm,
+                                           wad.data_ptr(), nwa, plan.err.data_ptr(), K.stream_handle()), "balance")
 
     def _phase(self, name, fn):
         if not self._use_graphs:
@@ -747,17 +776,14 @@ class KronWhiten:
             plan.run_apply(trace)
 
         run = (lambda name, fn: self._phase(name, fn)) if use_graph else (lambda name, fn: fn())
+        fired = [k for k, c in enumerate(coins) if c]
         if update and self.update_preconditioner_first:
             run("update", upd)
-            for k, c in enumerate(coins):
-                if c:
-                    self._balance(k)
+            self._balance(fired)
         run("apply", app)
         if update and not self.update_preconditioner_first:
             run("update", upd)
-            for k, c in enumerate(coins):
-                if c:
-                    self._balance(k)
+            self._balance(fired)
         self._steps += 1
 
     def _load_draws(self, normals):
