@@ -149,8 +149,15 @@ class ClockSampler:
                 for nm, v in zip(names, c[5:9]):
                     if v.lower().startswith("active"):
                         reasons.add(nm)
-        if not sm:
-            return None
+        if not sm:  # a timed region shorter than one sampling interval: take one reading now
+            try:
+                out = subprocess.run(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-i",
+                                      str(self.idx)], capture_output=True, text=True, timeout=10).stdout
+                c = [x.strip() for x in out.strip().split(",")]
+                sm, smax = [float(c[1])], [float(c[2])]
+                reasons = {nm for nm, v in zip(names, c[5:9]) if v.lower().startswith("active")}
+            except Exception:
+                return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
                 "samples": len(sm)}
 

@@ -112,7 +112,12 @@ class ShardedKronWhiten:
 
     @torch.no_grad()
     def step_math(self, grads, draws=None):
+        """grads: one per parameter (all ranks pass the full list). draws (tests): the full draw set of
+        KronWhiten.step_math; this rank keeps the coins and normals of its own parameters."""
         grads = list(grads)
+        if draws is not None:
+            draws = {"update": draws["update"], "coins": [draws["coins"][i] for i in self.owned] if draws["coins"] else [],
+                     "normals": [draws["normals"][i] for i in self.owned] if draws["normals"] else []}
         if self.opt is not None:
             self.opt.step_math([grads[i] for i in self.owned], draws=draws)
         self.allgather()
