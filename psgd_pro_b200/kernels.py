@@ -99,3 +99,35 @@ class GemmGroup:
     def launch(self, err):
         check(_capi.lib().psgd_gemm_launch(self.table.data_ptr(), self.tiles.data_ptr(), self.ntiles, self.split,
                                            self.kind, ptr(err), stream_handle()), "psgd_gemm_launch")
+
+
+def _prep_one(item_fields, rows, cols, normal):
+    """One psgd_prep launch for a single item (plug-in helpers; item and work list uploaded per call)."""
+    it = _capi.PrepItem()
+    for k, v in item_fields.items():
+        setattr(it, k, v)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    host = torch.empty(ctypes.sizeof(it), dtype=torch.uint8)
+    ctypes.memmove(host.data_ptr(), ctypes.addressof(it), ctypes.sizeof(it))
+    items = host.to(dev)
+    if normal:
+        pairs = [(0, rb) for rb in range((rows + _capi.PREP_ROWS - 1) // _capi.PREP_ROWS)]
+    else:
+        pairs = [(0, (ti << 16) | tj) for ti in range((rows + 31) // 32) for tj in range((cols + 31) // 32)]
+    work = torch.tensor([v for p in pairs for v in p], dtype=torch.int32).to(dev)
+    hyper = torch.zeros(_capi.HY_COUNT, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    check(_capi.lib().psgd_prep(items.data_ptr(), work.data_ptr(), len(pairs), hyper.data_ptr(), err.data_ptr(),
+                                stream_handle()), "psgd_prep")
+    return (items, work, hyper, err)  # kept alive by the caller until the launch has run
+
+
+def to_operand(X, transpose=False, split=True):
+    """(hi, lo) bf16 operand of the fp32 / bf16 matrix X (or of X^T), staged by the psgd_prep kernel."""
+    X = X.contiguous()
+    r, c = X.shape
+    hi, lo = operand(c, r, X.device, split) if transpose else operand(r, c, X.device, split)
+    keep = _prep_one(dict(g=X.data_ptr(), g_bf16=int(X.dtype == BF16), mode=_capi.PSGD_PREP_TRANS if transpose
+                          else _capi.PSGD_PREP_NORMAL, xi=None, n1=r, n2=c, p1=None, p2=None, out_hi=ptr(hi),
+                          out_lo=ptr(lo), ld_out=hi.stride(0), eps=0.0), r, c, not transpose)
+    return (hi, lo), keep
