@@ -16,6 +16,8 @@
 #include <float.h>
 #include <stdio.h>
 #include <string.h>
+#include <queue>
+#include <type_traits>
 #include <vector>
 
 namespace psgd {
@@ -422,15 +424,17 @@ __device__ __forceinline__ void epilogue_tile(const GemmDesc& d, int tm, int tn,
 }
 
 // ---- fast epilogue for interior tiles -------------------------------------------------------------------------------
-// Interior tiles (all 128 rows and bn columns inside the matrix; for SYRK, tiles strictly above the diagonal) of
-// problems whose pointers and leading dimensions allow vector accesses take a specialised path per epilogue kind:
-// no per-element masks, no tail handling, one instruction stream per kind. Same lane mappings, staging and fixed
-// reduction order as epilogue_tile.
+// Interior tiles (all 128 rows and bn columns inside the matrix) of problems whose pointers and leading dimensions
+// allow vector accesses take a specialised path per epilogue kind: no tail handling, one instruction stream per
+// kind. The column pass is epilogue_tile's; the transposed pass keeps one accumulator row per lane (the TMEM
+// layout) so each warp store writes 32 consecutive elements of a transposed row, and reads no shared memory in
+// SYRK mode. SYRK tiles that meet the diagonal mask only the one 32 x 32 chunk per warp that the diagonal crosses.
 enum : int { EPI_GENERIC = 0, EPI_AUX = 1, EPI_NLB = 2, EPI_PLAIN = 3, EPI_SYRK = 4 };
 
-template <int KIND, int BNMAX>
+template <int KIND, int BNMAX, bool DG>
 __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn, uint32_t tacc, int q, int lane, float* red,
                               float* cs, float* misc, float* stage) {
+  static_assert(!DG || KIND == EPI_SYRK, "diagonal tiles exist in SYRK mode only");
   const PsgdGemmSpec& sd = d.s;
   const long long s_M = sd.M, s_N = sd.N;
   const int bn = sd.bn;
@@ -451,6 +455,7 @@ __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn,
   const float* __restrict__ s_dot = sd.dot_aux;
   const long long s_ld_dot = sd.ld_dot;
   float* __restrict__ s_part_dot = sd.part_dot;
+  float* __restrict__ s_diag_out = sd.diag_out;
   const int d_tiles_n = d.tiles_n;
   const long long m0 = (long long)tm * BM, n0 = (long long)tn * bn;
   const long long row0 = m0 + q * 32;
@@ -472,26 +477,45 @@ __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn,
   }
   named_sync(1, 128);
 
-  const int rs = lane >> 3, cg = lane & 7;     // column pass: rows rs + 4 it, columns 4 cg .. 4 cg + 3
-  const int cs_ = lane >> 3, rg = lane & 7;    // transposed pass: column 4 it + cs_, rows 4 rg .. 4 rg + 3
+  const int rs = lane >> 3, cg = lane & 7;  // column pass: rows rs + 4 it, columns 4 cg .. 4 cg + 3
+  const long long rr = row0 + lane;         // transposed pass: one accumulator row per lane
   float rowacc[8];
 #pragma unroll
   for (int it = 0; it < 8; ++it) rowacc[it] = 0.f;
   float tsum = 0.f, dsum = 0.f;
+  // The column-pass operand (aux, or the trace operand in SYRK mode) of the next chunk is requested while the
+  // current one is processed.
   const float* pre_src = KIND == EPI_AUX ? s_aux : (KIND == EPI_SYRK ? s_dot : nullptr);
   const long long pre_ld = KIND == EPI_AUX ? s_ld_aux : s_ld_dot;
-  for (int c0 = 0; c0 < bn; c0 += 32) {
-    float4 pv[8];  // the chunk's aux / trace operand, issued before the TMEM load so their latencies overlap
-    if (pre_src) {
+  // The transposed pass reads the transformed values back from the staging block, except in SYRK mode where they
+  // are alpha times the accumulator registers themselves.
+  const bool writeback = KIND != EPI_SYRK && ht != nullptr;
+  // SYRK tiles on the diagonal: for this warp's 32 rows the chunks left of column row0 hold no direct or mirrored
+  // element (every offset is a multiple of 32), the chunk starting at row0 is masked per element (MASK), and the
+  // chunks to its right are above the diagonal.
+  const int c_first = DG ? (int)(row0 - n0) : 0;
+  float4 pv[8];
+  if (pre_src) {
 #pragma unroll
-      for (int it = 0; it < 8; ++it)
-        pv[it] = *reinterpret_cast<const float4*>(pre_src + (row0 + rs + 4 * it) * pre_ld + n0 + c0 + 4 * cg);
-    }
-    float v[32];
-    tmem_ld32(tacc + (uint32_t)c0, v);
+    for (int it = 0; it < 8; ++it)
+      pv[it] = *reinterpret_cast<const float4*>(pre_src + (row0 + rs + 4 * it) * pre_ld + n0 + c_first + 4 * cg);
+  }
+  if (DG && s_part_row && rs == 0) {  // the skipped chunks' column sums of squares are zero
+    for (int c0 = 0; c0 < c_first; c0 += 32)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) red[q * BNMAX + c0 + 4 * cg + i] = 0.f;
+  }
+
+  auto chunk = [&](const int c0, auto mask_tag) {
+    constexpr bool MASK = decltype(mask_tag)::value;
+    uint32_t ra[32];
+    tmem_ld32_issue(tacc + (uint32_t)c0, ra);
+    tmem_ld32_wait(ra);
 #pragma unroll
     for (int j = 0; j < 32; j += 4)
-      *reinterpret_cast<float4*>(stage + lane * STG + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+      *reinterpret_cast<float4*>(stage + lane * STG + j) =
+          make_float4(__uint_as_float(ra[j]), __uint_as_float(ra[j + 1]), __uint_as_float(ra[j + 2]),
+                      __uint_as_float(ra[j + 3]));
     __syncwarp();
     const long long colb = n0 + c0 + 4 * cg;
     float csc[4] = {1.f, 1.f, 1.f, 1.f};
@@ -536,7 +560,7 @@ __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn,
         if (s_out_f32)
           *reinterpret_cast<float4*>(s_out_f32 + row * s_ld_f32 + colb) = make_float4(x[0], x[1], x[2], x[3]);
         if (out_hi) st4b(out_hi + row * s_ld_b + colb, out_lo ? out_lo + row * s_ld_b + colb : nullptr, x, 4, true);
-      } else {  // EPI_SYRK, strictly upper tile: every element is direct and has a mirror
+      } else if (!MASK) {  // EPI_SYRK above the diagonal: every element is direct and has a mirror
         float rp = 0.f;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -544,13 +568,38 @@ __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn,
           rp += x2;
           csq[i] += x2;
         }
+        tsum += rp;
         rowacc[it] += rp;
         if (s_out_f32)
           *reinterpret_cast<float4*>(s_out_f32 + row * s_ld_f32 + colb) = make_float4(x[0], x[1], x[2], x[3]);
         if (out_hi) st4b(out_hi + row * s_ld_b + colb, out_lo ? out_lo + row * s_ld_b + colb : nullptr, x, 4, true);
         if (s_dot) dsum += x[0] * pv[it].x + x[1] * pv[it].y + x[2] * pv[it].z + x[3] * pv[it].w;
+      } else {  // EPI_SYRK on the diagonal: element i is direct when colb + i >= row, mirrored when >
+        const int first = (int)max(-1LL, min(4LL, row - colb));
+        const float dd[4] = {pv[it].x, pv[it].y, pv[it].z, pv[it].w};
+        float rp = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float x2 = x[i] * x[i];
+          const bool direct = i >= first;
+          rp += direct ? x2 : 0.f;
+          if (s_dot) dsum += direct ? x[i] * dd[i] : 0.f;
+          csq[i] += (i > first) ? x2 : 0.f;
+          if (i == first && s_diag_out) s_diag_out[row] = x[i];
+          if (direct) {
+            if (s_out_f32) s_out_f32[row * s_ld_f32 + colb + i] = x[i];
+            if (out_hi) {
+              __nv_bfloat16 h, l;
+              split_bf16(x[i], h, l);
+              out_hi[row * s_ld_b + colb + i] = h;
+              if (out_lo) out_lo[row * s_ld_b + colb + i] = l;
+            }
+          }
+        }
+        tsum += rp;
+        rowacc[it] += rp;
       }
-      *reinterpret_cast<float4*>(stage + r * STG + 4 * cg) = make_float4(x[0], x[1], x[2], x[3]);
+      if (writeback) *reinterpret_cast<float4*>(stage + r * STG + 4 * cg) = make_float4(x[0], x[1], x[2], x[3]);
     }
     if ((KIND == EPI_NLB || KIND == EPI_PLAIN) ? (s_part_col != nullptr) : (KIND == EPI_SYRK && s_part_row)) {
 #pragma unroll
@@ -565,35 +614,71 @@ __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn,
         for (int i = 0; i < 4; ++i) red[q * BNMAX + c0 + 4 * cg + i] = csq[i];
     }
     __syncwarp();
-    // transposed pass
-    __nv_bfloat16* th = KIND == EPI_SYRK ? out_hi : ht;
-    __nv_bfloat16* tl = KIND == EPI_SYRK ? out_lo : lt;
-    const long long tld = KIND == EPI_SYRK ? s_ld_b : s_ld_bt;
-    if (th || (KIND == EPI_SYRK && (s_out_f32 || s_dot))) {
-      const long long r0g = row0 + 4 * rg;
-      float4 md[8];
-      if (KIND == EPI_SYRK && s_dot) {
+    if (pre_src && c0 + 32 < bn) {  // the next chunk's column-pass operand
 #pragma unroll
-        for (int it = 0; it < 8; ++it)
-          md[it] = *reinterpret_cast<const float4*>(s_dot + (n0 + c0 + 4 * it + cs_) * s_ld_dot + r0g);
+      for (int it = 0; it < 8; ++it)
+        pv[it] = *reinterpret_cast<const float4*>(pre_src + (row0 + rs + 4 * it) * pre_ld + n0 + c0 + 32 + 4 * cg);
+    }
+    // transposed pass: the chunk's column j goes to row n0 + c0 + j of the transposed output (for SYRK, the
+    // mirror), so each warp store covers 32 consecutive rows: 64 contiguous bytes (bf16) or 128 (fp32).
+    if (KIND == EPI_SYRK) {
+      if (out_hi) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const long long col = n0 + c0 + j;
+          if (MASK && col <= rr) continue;  // on the diagonal only elements with col > row have a mirror
+          __nv_bfloat16 h, l;
+          split_bf16(alpha * __uint_as_float(ra[j]), h, l);
+          out_hi[col * s_ld_b + rr] = h;
+          if (out_lo) out_lo[col * s_ld_b + rr] = l;
+        }
+      }
+      if (s_out_f32) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const long long col = n0 + c0 + j;
+          if (MASK && col <= rr) continue;
+          s_out_f32[col * s_ld_f32 + rr] = alpha * __uint_as_float(ra[j]);
+        }
+      }
+      if (s_dot) {
+        float qv[32];  // all requested before the first use
+#pragma unroll
+        for (int j = 0; j < 32; ++j) qv[j] = __ldg(s_dot + (n0 + c0 + j) * s_ld_dot + rr);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float t = (alpha * __uint_as_float(ra[j])) * qv[j];
+          dsum += (MASK && n0 + c0 + j <= rr) ? 0.f : t;
+        }
+      }
+    } else if (ht) {
+      __syncwarp();
+      float y[32];
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 t = *reinterpret_cast<const float4*>(stage + lane * STG + j);
+        y[j] = t.x;
+        y[j + 1] = t.y;
+        y[j + 2] = t.z;
+        y[j + 3] = t.w;
       }
 #pragma unroll
-      for (int it = 0; it < 8; ++it) {
-        const int c = 4 * it + cs_;
-        const long long col = n0 + c0 + c;
-        float x[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) x[i] = stage[(4 * rg + i) * STG + c];
-        if (th) st4b(th + col * tld + r0g, tl ? tl + col * tld + r0g : nullptr, x, 4, true);
-        if (KIND == EPI_SYRK) {
-          if (s_out_f32)
-            *reinterpret_cast<float4*>(s_out_f32 + col * s_ld_f32 + r0g) = make_float4(x[0], x[1], x[2], x[3]);
-          if (s_dot) dsum += x[0] * md[it].x + x[1] * md[it].y + x[2] * md[it].z + x[3] * md[it].w;
-        }
+      for (int j = 0; j < 32; ++j) {
+        __nv_bfloat16 h, l;
+        split_bf16(y[j], h, l);
+        ht[(n0 + c0 + j) * s_ld_bt + rr] = h;
+        if (lt) lt[(n0 + c0 + j) * s_ld_bt + rr] = l;
       }
     }
     __syncwarp();
+  };
+
+  int c0 = c_first;
+  if (DG) {
+    chunk(c0, std::integral_constant<bool, true>());
+    c0 += 32;
   }
+  for (; c0 < bn; c0 += 32) chunk(c0, std::integral_constant<bool, false>());
 
   // ---- reductions (fixed order, as epilogue_tile) ----
 #pragma unroll
@@ -631,6 +716,11 @@ __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn,
   }
   named_sync(1, 128);
 }
+
+// Grouped tile lists start with a header of uint32 values: the number of segments S (one per CTA), then S + 1
+// offsets; segment b holds the tiles of CTA b, entries [off_b, off_(b+1)) of the (problem, tm << 16 | tn) pairs
+// that follow the header.
+PSGD_HD int tile_header_pairs(int nseg) { return (nseg + 3) / 2; }
 
 // Tile t of a launch: from the explicit list (grouped launch) or, with no list, the t-th tile of problem 0 in
 // row-major order (upper tiles only for SYRK).
@@ -678,6 +768,16 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
   float* stage_all = misc + 32;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // This CTA's tiles: a segment of the grouped tile list (per-CTA offsets in its header), or every gridDim-th tile
+  // of the single problem.
+  int t_begin = blockIdx.x, t_end = ntiles, t_step = gridDim.x;
+  if (tiles) {
+    const int nseg = (int)tiles[0];
+    t_begin = blockIdx.x < nseg ? (int)tiles[1 + blockIdx.x] : 0;
+    t_end = blockIdx.x < nseg ? (int)tiles[2 + blockIdx.x] : 0;
+    t_step = 1;
+    tiles += 2 * tile_header_pairs(nseg);
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -708,7 +808,7 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
       uint32_t armed[STAGES];  // phases armed per stage, to drain in-flight copies on abort
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) armed[s] = 0;
-      for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x) {
+      for (int t = t_begin; t < t_end && !*abort; t += t_step) {
         int p, tm, tn;
         get_tile(descs, tiles, t, p, tm, tn);
         const GemmDesc& d = descs[p];
@@ -743,7 +843,7 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
       // ---------------- MMA issuer ----------------
       uint32_t g = 0, i = 0;
       bool issued = false;
-      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+      for (int t = t_begin; t < t_end; t += t_step, ++i) {
         int p, tm, tn;
         get_tile(descs, tiles, t, p, tm, tn);
         const GemmDesc& d = descs[p];
@@ -790,7 +890,7 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
     // ---------------- epilogue (warps 2..5) ----------------
     const int q = warp & 3;
     uint32_t i = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+    for (int t = t_begin; t < t_end; t += t_step, ++i) {
       int p, tm, tn;
       get_tile(descs, tiles, t, p, tm, tn);
       const GemmDesc& d = descs[p];
@@ -809,9 +909,15 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
       const bool interior = m0 + BM <= d.s.M && n0 + d.s.bn <= d.s.N;
       // the launch's kind (template) picks the one fast path compiled into this kernel; problems of another
       // kind, edge tiles and SYRK tiles on the diagonal take the generic epilogue
-      const bool fast = KIND != EPI_GENERIC && d.fast == KIND && interior && (KIND != EPI_SYRK || n0 >= m0 + BM);
-      if (fast) epilogue_fast<KIND, BNMAX>(d, tm, tn, tacc, q, lane, red, cs, misc, stg);
-      else epilogue_tile<BNMAX>(d, tm, tn, tacc, q, lane, red, cs, misc, stg);
+      const bool fast = KIND != EPI_GENERIC && d.fast == KIND && interior;
+      if constexpr (KIND == EPI_SYRK) {
+        if (fast && n0 >= m0 + BM) epilogue_fast<KIND, BNMAX, false>(d, tm, tn, tacc, q, lane, red, cs, misc, stg);
+        else if (fast) epilogue_fast<KIND, BNMAX, true>(d, tm, tn, tacc, q, lane, red, cs, misc, stg);
+        else epilogue_tile<BNMAX>(d, tm, tn, tacc, q, lane, red, cs, misc, stg);
+      } else {
+        if (fast) epilogue_fast<KIND, BNMAX, false>(d, tm, tn, tacc, q, lane, red, cs, misc, stg);
+        else epilogue_tile<BNMAX>(d, tm, tn, tacc, q, lane, red, cs, misc, stg);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -984,7 +1090,7 @@ static int launch_group(const GemmDesc* descs, const uint32_t* tiles, int ntiles
   using C = GemmCfg<SPLIT, BNMAX, STAGES>;
   auto k = gemm_group_kernel<SPLIT, BNMAX, STAGES, KIND>;
   if (!smem_attr_once(reinterpret_cast<const void*>(k), C::SMEM_BYTES)) return PSGD_ELAUNCH;
-  const int grid = ntiles < num_sms() ? ntiles : num_sms();
+  const int grid = num_sms();  // one CTA per segment of the tile list
   k<<<grid, GEMM_THREADS, C::SMEM_BYTES, st>>>(descs, tiles, ntiles, err);
   return cudaGetLastError() == cudaSuccess ? PSGD_OK : PSGD_ELAUNCH;
 }
@@ -1032,12 +1138,26 @@ extern "C" size_t psgd_gemm_table_bytes(int nspecs) { return (size_t)(nspecs > 0
 
 extern "C" int psgd_gemm_count_tiles(const PsgdGemmSpec* specs, int nspecs) {
   if (!specs || nspecs < 0) return PSGD_EINVAL;
-  long long n = 0;
+  long long n = tile_header_pairs(num_sms());
   for (int i = 0; i < nspecs; ++i) {
     if (specs[i].M < 1 || specs[i].N < 1 || !valid_bn(specs[i].bn, 1)) return PSGD_EINVAL;
     n += spec_tiles(specs[i]);
   }
   return n > 0x7fffffff ? PSGD_EINVAL : (int)n;
+}
+
+// Estimated cycles a tile holds its CTA: the slower of its MMAs (one 128 x 256 x 64 block step ~730 cycles at the
+// tensor-core rate, three MMAs per step in split mode) and its epilogue (per 32-column chunk; the general epilogue
+// is several times dearer than the specialised ones). The accumulators are double-buffered, so the two overlap.
+static double tile_cost(const GemmDesc& d, int tm, int tn, int kind) {
+  const PsgdGemmSpec& s = d.s;
+  const double nk = (double)((s.K + BK - 1) / BK);
+  const double mma = nk * 730.0 * (s.bn / 256.0) * ((s.a_lo && s.b_lo) ? 3.0 : 1.0) + 1500.0;
+  const long long m0 = (long long)tm * BM, n0 = (long long)tn * s.bn;
+  const bool interior = m0 + BM <= s.M && n0 + s.bn <= s.N;
+  const bool fast = kind != EPI_GENERIC && d.fast == kind && interior;
+  const double epi = (s.bn / 32.0) * (fast ? 3000.0 : 12000.0);
+  return mma > epi ? mma : epi;
 }
 
 extern "C" int psgd_gemm_encode(const PsgdGemmSpec* specs, int nspecs, void* host_table, size_t table_bytes,
@@ -1055,9 +1175,6 @@ extern "C" int psgd_gemm_encode(const PsgdGemmSpec* specs, int nspecs, void* hos
     const int rc = fill_desc(&descs[i], specs[i], split == 3 && specs[i].bn > 128 ? 1 : split);
     if (rc) return rc;
   }
-  int k = 0;
-  for (int i = 0; i < nspecs; ++i) append_tiles(specs[i], (uint32_t)i, host_tiles, k);
-  *ntiles = k;
   // the group's epilogue kind: the fast kind covering the most tiles (its problems take the fast path)
   long long w[5] = {0, 0, 0, 0, 0};
   for (int i = 0; i < nspecs; ++i) w[descs[i].fast] += spec_tiles(specs[i]);
@@ -1065,6 +1182,46 @@ extern "C" int psgd_gemm_encode(const PsgdGemmSpec* specs, int nspecs, void* hos
   for (int t = 1; t < 5; ++t)
     if (w[t] > w[best] || (best == EPI_GENERIC && w[t] > 0)) best = t;
   *kind = best;
+
+  // Tiles in their natural order (problems as given, row-major within each), each handed to the CTA with the
+  // least estimated work so far: neighbouring tiles (which share operand panels in L2) run at about the same
+  // time, and costly tiles (long K, the general epilogue) do not pile up on a few CTAs.
+  const int nseg = num_sms();
+  const int hdr = tile_header_pairs(nseg);
+  std::vector<uint32_t> all;
+  all.reserve(2 * (size_t)(need - hdr));
+  for (int i = 0; i < nspecs; ++i) {
+    int k = 0;
+    std::vector<uint32_t> one(2 * (size_t)spec_tiles(specs[i]));
+    append_tiles(specs[i], (uint32_t)i, one.data(), k);
+    all.insert(all.end(), one.begin(), one.end());
+  }
+  const int nt = (int)(all.size() / 2);
+  std::vector<double> load(nseg, 0.0);
+  std::vector<int> owner(nt), count(nseg, 0);
+  std::priority_queue<std::pair<double, int>, std::vector<std::pair<double, int>>, std::greater<std::pair<double, int>>> pq;
+  for (int b = 0; b < nseg; ++b) pq.push({0.0, b});
+  for (int t = 0; t < nt; ++t) {
+    const auto top = pq.top();
+    pq.pop();
+    const int p = (int)all[2 * t], tm = (int)(all[2 * t + 1] >> 16), tn = (int)(all[2 * t + 1] & 0xFFFF);
+    owner[t] = top.second;
+    count[top.second] += 1;
+    pq.push({top.first + tile_cost(descs[p], tm, tn, best), top.second});
+  }
+  uint32_t* h = host_tiles;  // header: nseg, then nseg + 1 offsets
+  h[0] = (uint32_t)nseg;
+  h[1] = 0;
+  for (int b = 0; b < nseg; ++b) h[2 + b] = h[1 + b] + (uint32_t)count[b];
+  if (nseg + 2 < 2 * hdr) h[2 * hdr - 1] = 0;
+  std::vector<uint32_t> pos(h + 1, h + 1 + nseg);
+  uint32_t* body = host_tiles + 2 * hdr;
+  for (int t = 0; t < nt; ++t) {
+    const uint32_t j = pos[owner[t]]++;
+    body[2 * j] = all[2 * t];
+    body[2 * j + 1] = all[2 * t + 1];
+  }
+  *ntiles = hdr + nt;
   return PSGD_OK;
 }
 

@@ -58,7 +58,8 @@ def test_split_fp32(cuda, M, N, Kd, bn):
 
 
 @pytest.mark.parametrize("n,Kd,split,bn", [(128, 64, 1, 128), (384, 200, 3, 128), (300, 1000, 1, 128),
-                                          (10, 7, 3, 128), (600, 300, 1, 256), (1030, 64, 1, 256), (256, 96, 1, 256)])
+                                          (10, 7, 3, 128), (600, 300, 1, 256), (1030, 64, 1, 256), (256, 96, 1, 256),
+                                          (512, 256, 1, 256), (768, 128, 3, 128), (1024, 64, 1, 256)])
 def test_syrk_symmetric(cuda, n, Kd, split, bn):
     g = torch.Generator().manual_seed(n)
     x, X = bf16_operand(n, Kd, cuda, g, split=split == 3)
