@@ -179,9 +179,11 @@ int psgd_factor_update(const PsgdFactorItem* items, int nitems, const float* hyp
                        cudaStream_t stream);
 
 /* Rn = Q - Q^T (psgd_pro_fast.py:147; psgd_pro.py:87 up to sign), written as bf16 hi/lo. Work entries are
- * 32 x 32 tile pairs (ti <= tj): one block reads Q[ti, tj] and Q[tj, ti] once and writes both Rn tiles, with
- * part_row[slot][i] (row sums of squares; the slot is the column tile), and per pair part_max (max |Rn|) and
- * part_dot (sum Rn * Q) in entry ti * tiles + tj (entries with ti > tj stay zero). */
+ * pairs of PSGD_SKEW_TILE-square tiles (TI <= TJ): one block reads Q[TI, TJ] and Q[TJ, TI] once and writes both
+ * Rn tiles. Reductions use 32-wide slots (tiles32 = ceil(n / 32)): part_row[slot][i] (row sums of squares over the
+ * block's columns, slot 2 TJ or 2 TI), and per pair part_max (max |Rn|) and part_dot (sum Rn * Q) in entry
+ * (2 TI) * tiles32 + 2 TJ. Every other slot stays as the caller left it (zero: consumers sum or max over all). */
+#define PSGD_SKEW_TILE 64
 typedef struct PsgdSkewItem {
   const float* q; int n;
   void* r_hi; void* r_lo; long long ldr;
@@ -191,7 +193,9 @@ int psgd_skew(const PsgdSkewItem* items, const uint32_t* work, int nwork, int* d
 
 /* M = a (Rn / s) + a^2 / 2 ((S / s) / s) (bf16 hi/lo in, bf16 hi/lo out in place of Rn), with a = *alpha and
  * 1/s = *beta from PSGD_FACTOR_SKEW: the Procrustes multiplier of psgd_pro_fast.py:153. Work entries: (item,
- * first row of a block of 4 rows); whole padded rows are processed (padding columns are zero and stay zero). */
+ * first row of a block of PSGD_ROT_ROWS rows); whole padded rows are processed (padding columns are zero and stay
+ * zero). */
+#define PSGD_ROT_ROWS 8
 typedef struct PsgdRotItem {
   int n;
   void* r_hi; void* r_lo; long long ldr;

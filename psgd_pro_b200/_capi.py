@@ -83,6 +83,8 @@ class BalanceParam(ctypes.Structure):
 
 PSGD_PREP_NORMAL, PSGD_PREP_TRANS, PSGD_PREP_DIRECT = 0, 1, 2
 PREP_ROWS = 8
+ROT_ROWS = 8
+SKEW_TILE = 64
 PSGD_FACTOR_DENSE, PSGD_FACTOR_RANK1, PSGD_FACTOR_DIAG, PSGD_FACTOR_SKEW = 0, 1, 2, 3
 HY_LR_PRECOND, HY_BETA_L, HY_DAMPING, HY_LR_PARAMS, HY_MAX_AVG, HY_MAX_ELEM, HY_MOM_BETA, HY_COUNT = range(8)
 APPLY_CHUNK = 8192

@@ -328,8 +328,13 @@ __global__ void __launch_bounds__(FAC_THREADS) factor_kernel(const PsgdFactorIte
 }
 
 // ---- Rn = Q - Q^T ------------------------------------------------------------------------------------------------
-// One block per tile pair (ti <= tj): tiles A = Q[ti, tj] and B = Q[tj, ti] are read once (float4 when n % 4 == 0)
-// and both Rn tiles, Rn[ti, tj] = A - B^T and Rn[tj, ti] = B - A^T, are written (8-byte bf16 stores).
+// One block per pair of 64 x 64 tiles (TI <= TJ): A = Q[TI, TJ] and B = Q[TJ, TI] are read once (a warp load
+// covers two 256-byte tile rows; float4 when n % 4 == 0), all requested before the first barrier, and both Rn
+// tiles, Rn[TI, TJ] = A - B^T and Rn[TJ, TI] = B - A^T, are written (8-byte bf16 stores). The reductions go to the
+// 32-wide slot layout of PsgdSkewItem: row sums into slot 2 TJ (or 2 TI), the pair's max and trace share into entry
+// (2 TI) * tiles32 + 2 TJ; the slots no block writes stay zero.
+constexpr int SK = PSGD_SKEW_TILE;
+
 PSGD_DEVI void st4_split(void* hi, void* lo, long long idx, const float* x, bool vec, int nvalid) {
   __align__(8) __nv_bfloat16 h[4], l[4];
 #pragma unroll
@@ -347,85 +352,99 @@ PSGD_DEVI void st4_split(void* hi, void* lo, long long idx, const float* x, bool
   }
 }
 
+// Q[row][col0 .. col0 + 3] (zero outside the matrix).
+PSGD_DEVI float4 load4q(const float* __restrict__ q, int n, int row, int col0, bool vec) {
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (row >= n) return v;
+  const float* src = q + (long long)row * n + col0;
+  if (vec && col0 + 3 < n) return *reinterpret_cast<const float4*>(src);
+  if (col0 < n) v.x = src[0];
+  if (col0 + 1 < n) v.y = src[1];
+  if (col0 + 2 < n) v.z = src[2];
+  if (col0 + 3 < n) v.w = src[3];
+  return v;
+}
+
 __global__ void __launch_bounds__(256) skew_kernel(const PsgdSkewItem* __restrict__ items,
                                                   const uint32_t* __restrict__ work, int nwork) {
-  __shared__ float sA[TT][TT + 1], sB[TT][TT + 1];
+  __shared__ float sA[SK][SK + 1], sB[SK][SK + 1];
   __shared__ float red[8][2];
   const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
-  const int r = t >> 3, c4 = (t & 7) * 4;  // this thread: row r, columns c4 .. c4 + 3 of a tile
+  const int rr = t >> 4, c4 = (t & 15) * 4;  // this thread: rows rr + 16 m, columns c4 .. c4 + 3 of a tile
   for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
     const PsgdSkewItem& it = items[work[2 * w]];
     const int ti = work[2 * w + 1] >> 16, tj = work[2 * w + 1] & 0xFFFF;
-    const int n = it.n, i0 = ti * TT, j0 = tj * TT;
+    const int n = it.n, i0 = ti * SK, j0 = tj * SK;
     const bool diag = ti == tj;
     const bool vec = (n % 4) == 0;
-    // load A (rows i0.., cols j0..) and B (rows j0.., cols i0..)
-    {
-      const int ia = i0 + r, ja = j0 + c4, ib = j0 + r, jb = i0 + c4;
-      float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
-      if (ia < n) {
-        if (vec && ja + 3 < n) {
-          const float4 v = *reinterpret_cast<const float4*>(it.q + (long long)ia * n + ja);
-          a[0] = v.x; a[1] = v.y; a[2] = v.z; a[3] = v.w;
-        } else {
-          for (int k = 0; k < 4; ++k) if (ja + k < n) a[k] = it.q[(long long)ia * n + ja + k];
-        }
-      }
-      if (!diag && ib < n) {
-        if (vec && jb + 3 < n) {
-          const float4 v = *reinterpret_cast<const float4*>(it.q + (long long)ib * n + jb);
-          b[0] = v.x; b[1] = v.y; b[2] = v.z; b[3] = v.w;
-        } else {
-          for (int k = 0; k < 4; ++k) if (jb + k < n) b[k] = it.q[(long long)ib * n + jb + k];
-        }
-      }
+    float4 a[4], b[4];  // this thread's rows of A and B: the untransposed operands of the differences below
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        sA[r][c4 + k] = a[k];
-        sB[r][c4 + k] = b[k];
+    for (int m = 0; m < 4; ++m) {
+      a[m] = load4q(it.q, n, i0 + rr + 16 * m, j0 + c4, vec);
+      b[m] = diag ? a[m] : load4q(it.q, n, j0 + rr + 16 * m, i0 + c4, vec);
+    }
+    {
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const int r = rr + 16 * m;
+        sA[r][c4] = a[m].x;
+        sA[r][c4 + 1] = a[m].y;
+        sA[r][c4 + 2] = a[m].z;
+        sA[r][c4 + 3] = a[m].w;
+        sB[r][c4] = b[m].x;
+        sB[r][c4 + 1] = b[m].y;
+        sB[r][c4 + 2] = b[m].z;
+        sB[r][c4 + 3] = b[m].w;
       }
     }
     __syncthreads();
-    if (diag) {
-#pragma unroll
-      for (int k = 0; k < 4; ++k) sB[r][c4 + k] = sA[r][c4 + k];
-      __syncthreads();
-    }
     float mx = 0.f, dsum = 0.f;
-    const int tiles = (n + TT - 1) / TT;
+    const int tiles32 = (n + 31) / 32;
     for (int half = 0; half < (diag ? 1 : 2); ++half) {
-      // half 0: Rn[ti, tj] rows i0 + r = A[r][c] - B[c][r]; half 1: Rn[tj, ti] rows j0 + r = B[r][c] - A[c][r]
-      const float(*X)[TT + 1] = half == 0 ? sA : sB;
-      const float(*Y)[TT + 1] = half == 0 ? sB : sA;
-      const int gi = (half == 0 ? i0 : j0) + r, gj0 = (half == 0 ? j0 : i0) + c4;
-      float v[4], rs = 0.f;
+      // half 0: Rn[TI, TJ] rows i0 + r = A[r][c] - B[c][r]; half 1: Rn[TJ, TI] rows j0 + r = B[r][c] - A[c][r]
+      const float(*Y)[SK + 1] = half == 0 ? sB : sA;
+      const int gr0 = half == 0 ? i0 : j0, gj0 = (half == 0 ? j0 : i0) + c4;
+      const int slot = 2 * (half == 0 ? tj : ti);
+      const int nv = max(0, min(4, n - gj0));
+      const bool vs = nv == 4 && (it.ldr % 4) == 0;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const bool ok = gi < n && gj0 + k < n;
-        v[k] = ok ? X[r][c4 + k] - Y[c4 + k][r] : 0.f;
-        rs += v[k] * v[k];
-        mx = fmaxf(mx, fabsf(v[k]));
-        dsum += v[k] * X[r][c4 + k];
+      for (int m = 0; m < 4; ++m) {
+        const int r = rr + 16 * m, gi = gr0 + r;
+        const float4 xv = half == 0 ? a[m] : b[m];
+        const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
+        float v[4], rs = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const bool ok = gi < n && gj0 + k < n;
+          const float x = xs[k];
+          v[k] = ok ? x - Y[c4 + k][r] : 0.f;
+          rs += v[k] * v[k];
+          mx = fmaxf(mx, fabsf(v[k]));
+          dsum += v[k] * x;
+        }
+        if (gi < n && nv > 0) st4_split(it.r_hi, it.r_lo, (long long)gi * it.ldr + gj0, v, vs, nv);
+        rs += __shfl_xor_sync(0xffffffffu, rs, 1);
+        rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+        rs += __shfl_xor_sync(0xffffffffu, rs, 4);
+        rs += __shfl_xor_sync(0xffffffffu, rs, 8);
+        if ((t & 15) == 0 && gi < n) it.part_row[(long long)slot * n + gi] = rs;
       }
-      if (gi < n) {
-        const int nv = max(0, min(4, n - gj0));
-        if (nv > 0) st4_split(it.r_hi, it.r_lo, (long long)gi * it.ldr + gj0, v, nv == 4 && (it.ldr % 4) == 0, nv);
-      }
-      rs += __shfl_xor_sync(0xffffffffu, rs, 1);
-      rs += __shfl_xor_sync(0xffffffffu, rs, 2);
-      rs += __shfl_xor_sync(0xffffffffu, rs, 4);
-      const int slot = half == 0 ? tj : ti;
-      if ((t & 7) == 0 && gi < n) it.part_row[(long long)slot * n + gi] = rs;
     }
     mx = warp_max(mx);
     dsum = warp_sum(dsum);
-    if (lane == 0) { red[wid][0] = mx; red[wid][1] = dsum; }
+    if (lane == 0) {
+      red[wid][0] = mx;
+      red[wid][1] = dsum;
+    }
     __syncthreads();
     if (t == 0) {
       float m = 0.f, d = 0.f;
-      for (int k = 0; k < 8; ++k) { m = fmaxf(m, red[k][0]); d += red[k][1]; }
-      it.part_max[(long long)ti * tiles + tj] = m;  // the pair's max and trace share, in the (ti, tj) slot
-      it.part_dot[(long long)ti * tiles + tj] = d;
+      for (int k = 0; k < 8; ++k) {
+        m = fmaxf(m, red[k][0]);
+        d += red[k][1];
+      }
+      it.part_max[(long long)(2 * ti) * tiles32 + 2 * tj] = m;
+      it.part_dot[(long long)(2 * ti) * tiles32 + 2 * tj] = d;
     }
     __syncthreads();
   }
@@ -433,8 +452,10 @@ __global__ void __launch_bounds__(256) skew_kernel(const PsgdSkewItem* __restric
 
 // ---- M = a Rn / s + a^2 / 2 (S / s) / s ----------------------------------------------------------------------------
 // Rows of the padded n x ld bf16 arrays, 8 values (16 bytes) per vector; padding columns are zero and stay zero.
-// Work entries: (item, first row of a block of ROT_ROWS rows).
-constexpr int ROT_ROWS = 4;
+// Work entries: (item, first row of a block of ROT_ROWS rows). Each thread takes up to ROT_VEC vectors per pass
+// and requests all their inputs before the first use.
+constexpr int ROT_ROWS = PSGD_ROT_ROWS;
+constexpr int ROT_VEC = 4;
 
 PSGD_DEVI void unpack8(const uint4& u, float* f) {
   const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
@@ -449,33 +470,51 @@ __global__ void __launch_bounds__(256) rot_kernel(const PsgdRotItem* __restrict_
     const int r0 = (int)work[2 * w + 1];
     const float a = *it.alpha, inv_s = *it.beta, half_a2 = 0.5f * a * a;
     const int nvec = (int)(it.ldr / 8);
-    const int rows = min(ROT_ROWS, it.n - r0);
-    for (int k = threadIdx.x; k < rows * nvec; k += blockDim.x) {
-      const long long row = r0 + k / nvec, col = (long long)(k % nvec) * 8;
-      uint4* rh = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(it.r_hi) + row * it.ldr + col);
-      const uint4* sh = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(it.s_hi) + row * it.lds + col);
-      float rv[8], sv[8];
-      unpack8(*rh, rv);
-      unpack8(*sh, sv);
-      uint4* rl = nullptr;
-      if (it.r_lo) {
-        rl = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(it.r_lo) + row * it.ldr + col);
-        float l[8];
-        unpack8(*rl, l);
+    const int total = min(ROT_ROWS, it.n - r0) * nvec;
+    __nv_bfloat16* rbase_h = reinterpret_cast<__nv_bfloat16*>(it.r_hi);
+    __nv_bfloat16* rbase_l = reinterpret_cast<__nv_bfloat16*>(it.r_lo);
+    const __nv_bfloat16* sbase_h = reinterpret_cast<const __nv_bfloat16*>(it.s_hi);
+    const __nv_bfloat16* sbase_l = reinterpret_cast<const __nv_bfloat16*>(it.s_lo);
+    for (int k0 = threadIdx.x; k0 < total; k0 += ROT_VEC * blockDim.x) {
+      uint4 rh[ROT_VEC], sh[ROT_VEC], rl[ROT_VEC], sl[ROT_VEC];
+      long long ro[ROT_VEC], so[ROT_VEC];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) rv[i] += l[i];
+      for (int u = 0; u < ROT_VEC; ++u) {
+        const int k = k0 + u * blockDim.x;
+        const long long row = r0 + k / nvec, col = (long long)(k % nvec) * 8;
+        ro[u] = row * it.ldr + col;
+        so[u] = row * it.lds + col;
+        if (k < total) {
+          rh[u] = *reinterpret_cast<const uint4*>(rbase_h + ro[u]);
+          sh[u] = *reinterpret_cast<const uint4*>(sbase_h + so[u]);
+          if (rbase_l) rl[u] = *reinterpret_cast<const uint4*>(rbase_l + ro[u]);
+          if (sbase_l) sl[u] = *reinterpret_cast<const uint4*>(sbase_l + so[u]);
+        }
       }
-      if (it.s_lo) {
-        float l[8];
-        unpack8(*reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(it.s_lo) + row * it.lds + col), l);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) sv[i] += l[i];
+      for (int u = 0; u < ROT_VEC; ++u) {
+        if (k0 + u * blockDim.x >= total) continue;
+        float rv[8], sv[8];
+        unpack8(rh[u], rv);
+        unpack8(sh[u], sv);
+        if (rbase_l) {
+          float l[8];
+          unpack8(rl[u], l);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) rv[i] += l[i];
+        }
+        if (sbase_l) {
+          float l[8];
+          unpack8(sl[u], l);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) sv[i] += l[i];
+        }
+        __align__(16) __nv_bfloat16 h[8], l[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) split_bf16(a * (rv[i] * inv_s) + half_a2 * ((sv[i] * inv_s) * inv_s), h[i], l[i]);
+        *reinterpret_cast<uint4*>(rbase_h + ro[u]) = *reinterpret_cast<const uint4*>(h);
+        if (rbase_l) *reinterpret_cast<uint4*>(rbase_l + ro[u]) = *reinterpret_cast<const uint4*>(l);
       }
-      __align__(16) __nv_bfloat16 h[8], l[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) split_bf16(a * (rv[i] * inv_s) + half_a2 * ((sv[i] * inv_s) * inv_s), h[i], l[i]);
-      *rh = *reinterpret_cast<const uint4*>(h);
-      if (rl) *rl = *reinterpret_cast<const uint4*>(l);
     }
   }
 }
@@ -637,10 +676,15 @@ __global__ void __launch_bounds__(256) balance_apply_kernel(const PsgdBalanceFac
   }
 }
 
-static int grid_for(int nwork) {
-  int dev = 0, sms = 148;
+// Grid of a grid-stride kernel: every block resident at once (SMs x the blocks per SM that the kernel's registers
+// and shared memory allow), so no second partial wave runs its share of the work alone at the end.
+template <typename Kernel>
+static int grid_for(Kernel kernel, int threads, int nwork) {
+  int dev = 0, sms = 148, per_sm = 1;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int cap = sms * 8;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  const int cap = sms * per_sm;
   return nwork < cap ? nwork : cap;
 }
 
@@ -654,7 +698,7 @@ extern "C" int psgd_prep(const PsgdPrepItem* items, const uint32_t* work, int nw
                          cudaStream_t stream) {
   if (!items || !work || !hyper || nwork < 0) return PSGD_EINVAL;
   if (nwork == 0) return PSGD_OK;
-  prep_kernel<<<grid_for(nwork), 256, 0, stream>>>(items, work, nwork, hyper);
+  prep_kernel<<<grid_for(prep_kernel, 256, nwork), 256, 0, stream>>>(items, work, nwork, hyper);
   return launched();
 }
 
@@ -677,7 +721,7 @@ extern "C" int psgd_skew(const PsgdSkewItem* items, const uint32_t* work, int nw
                          cudaStream_t stream) {
   if (!items || !work || nwork < 0) return PSGD_EINVAL;
   if (nwork == 0) return PSGD_OK;
-  skew_kernel<<<grid_for(nwork), 256, 0, stream>>>(items, work, nwork);
+  skew_kernel<<<grid_for(skew_kernel, 256, nwork), 256, 0, stream>>>(items, work, nwork);
   return launched();
 }
 
@@ -685,7 +729,7 @@ extern "C" int psgd_rot(const PsgdRotItem* items, const uint32_t* work, int nwor
                         cudaStream_t stream) {
   if (!items || !work || nwork < 0) return PSGD_EINVAL;
   if (nwork == 0) return PSGD_OK;
-  rot_kernel<<<grid_for(nwork), 256, 0, stream>>>(items, work, nwork);
+  rot_kernel<<<grid_for(rot_kernel, 256, nwork), 256, 0, stream>>>(items, work, nwork);
   return launched();
 }
 
@@ -697,7 +741,7 @@ extern "C" int psgd_apply(const PsgdApplyItem* items, int nitems, const uint32_t
   int rc = launched();
   if (rc) return rc;
   if (nwork == 0) return PSGD_OK;
-  apply_kernel<<<grid_for(nwork), 256, 0, stream>>>(items, work, nwork, hyper);
+  apply_kernel<<<grid_for(apply_kernel, 256, nwork), 256, 0, stream>>>(items, work, nwork, hyper);
   return launched();
 }
 
@@ -706,11 +750,11 @@ extern "C" int psgd_balance(const PsgdBalanceFactor* factors, const PsgdBalanceP
                             int* dev_err, cudaStream_t stream) {
   if (!factors || !params || nparams < 0 || nwork_max < 0 || nwork_apply < 0) return PSGD_EINVAL;
   if (nparams == 0) return PSGD_OK;
-  if (nwork_max) absmax_kernel<<<grid_for(nwork_max), 256, 0, stream>>>(factors, work_max, nwork_max);
+  if (nwork_max) absmax_kernel<<<grid_for(absmax_kernel, 256, nwork_max), 256, 0, stream>>>(factors, work_max, nwork_max);
   int rc = launched();
   if (rc) return rc;
   balance_scale_kernel<<<nparams, 32, 0, stream>>>(factors, params);
   if ((rc = launched())) return rc;
-  if (nwork_apply) balance_apply_kernel<<<grid_for(nwork_apply), 256, 0, stream>>>(factors, work_apply, nwork_apply);
+  if (nwork_apply) balance_apply_kernel<<<grid_for(balance_apply_kernel, 256, nwork_apply), 256, 0, stream>>>(factors, work_apply, nwork_apply);
   return launched();
 }

@@ -338,7 +338,10 @@ class _Plan:
             it.q, it.n, it.r_hi, it.r_lo, it.ldr = f.q.data_ptr(), f.n, K.ptr(f.R[0]), K.ptr(f.R[1]), f.R[0].stride(0)
             it.part_row, it.part_max, it.part_dot = f.r_rows.data_ptr(), f.r_max.data_ptr(), f.r_dot.data_ptr()
             sk.append(it)
-            skw += [(len(sk) - 1, (ti << 16) | tj) for ti in range(f.T32) for tj in range(ti, f.T32)]
+            # pairs by diagonal (tj - ti, then ti): blocks running together read tiles at many row and column
+            # offsets, not one column band of Q (whose rows sit a power-of-two stride apart)
+            t64 = cdiv(f.n, _capi.SKEW_TILE)
+            skw += [(len(sk) - 1, (ti << 16) | (ti + d)) for d in range(t64) for ti in range(t64 - d)]
         self.skew_dev = _upload(_capi.SkewItem, sk, dev)
         self.skew_work, self.skew_n = _work(skw, dev)
         # U12..U16: norm lower bound of Rn (skew)
@@ -366,7 +369,7 @@ class _Plan:
             it.s_hi, it.s_lo, it.lds = K.ptr(f.T[0]), K.ptr(f.T[1]), f.T[0].stride(0)
             it.alpha, it.beta = self.s(f, S_AM).data_ptr(), self.s(f, S_BM).data_ptr()
             ri.append(it)
-            rw += [(len(ri) - 1, r0) for r0 in range(0, f.n, 4)]
+            rw += [(len(ri) - 1, r0) for r0 in range(0, f.n, _capi.ROT_ROWS)]
         self.rot_dev = _upload(_capi.RotItem, ri, dev)
         self.rot_work, self.rot_n = _work(rw, dev)
         # U20: Q <- Q - M Q

@@ -33,3 +33,13 @@ def test_spec_struct_size_matches_header():
     s = _capi.GemmSpec
     assert s.M.offset == 6 * 8 and s.alpha.offset == s.mode.offset + 4
     assert ctypes.sizeof(s) % 8 == 0
+
+
+def test_header_constants_match_binding():
+    """Work-list geometry the host encodes (row blocks, chunks) must be the one the kernels assume."""
+    text = open(HDR).read()
+    defs = dict(re.findall(r"#define (PSGD_\w+) (\d+)", text))
+    assert int(defs["PSGD_PREP_ROWS"]) == _capi.PREP_ROWS
+    assert int(defs["PSGD_ROT_ROWS"]) == _capi.ROT_ROWS
+    assert int(defs["PSGD_SKEW_TILE"]) == _capi.SKEW_TILE
+    assert int(defs["PSGD_APPLY_CHUNK"]) == _capi.APPLY_CHUNK
