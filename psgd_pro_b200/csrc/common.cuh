@@ -121,6 +121,79 @@ PSGD_DEVI void umma_commit(uint64_t* bar) {
                : "memory");
 }
 
+// ---- CTA pairs (clusters of two CTAs on neighbouring SMs, tcgen05 cta_group::2) -----------------------------
+PSGD_DEVI uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Every thread of both CTAs; release / acquire orders the shared-memory writes before it for the peer.
+PSGD_DEVI void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address of this CTA's shared variable `p` in the shared memory of CTA `rank` of the cluster.
+PSGD_DEVI uint32_t mapa_shared(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+// Arrive on a barrier of either CTA of the cluster (address from mapa_shared), releasing this thread's earlier
+// memory operations to the cluster.
+PSGD_DEVI void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+// The same without ordering: a pure signal (a release here would hold the producer until its copies in flight land).
+PSGD_DEVI void mbar_arrive_cluster_relaxed(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+// 2-D TMA tile load into this CTA's shared memory whose completion is counted on a barrier of either CTA of the
+// pair (the leader's, for the pair MMA). No multicast.
+PSGD_DEVI void tma_load_2d_pair(void* smem_dst, const CUtensorMap* tmap, uint32_t bar_cluster, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+
+// TMEM allocation for a pair: one warp of each CTA executes it; both get the same columns.
+PSGD_DEVI void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+PSGD_DEVI void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+PSGD_DEVI void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Pair MMA issued by the leader CTA: D (M = 256 rows, 128 in each CTA's TMEM) (+)= A B^T, A's rows and B's rows
+// split between the two CTAs' shared memory at the same offsets.
+PSGD_DEVI void umma_bf16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on the barrier at `bar`'s offset in each CTA of `mask` when the pair MMAs issued so far complete.
+PSGD_DEVI void umma_commit_pair(uint64_t* bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+      ::"r"(smem_u32(bar)), "h"(mask)
+      : "memory");
+}
+
 // Shared-memory matrix descriptor for a K-major tile written by TMA with 128-byte swizzling: rows of 128 bytes
 // (64 bf16), 8-row swizzle atoms of 1024 bytes stacked densely (stride-dimension offset 1024 B). The tile base
 // must be 1024-byte aligned; stepping K inside the atom adds the byte offset to the start address.
@@ -137,6 +210,10 @@ PSGD_DEVI uint64_t sdesc_k_sw128(uint32_t saddr) {
 // Instruction descriptor: bf16 x bf16 -> fp32, A and B K-major, M = 128, N = n (multiple of 16, <= 256).
 PSGD_DEVI uint32_t idesc_bf16_m128(int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+// The same for the pair MMA (M = 256).
+PSGD_DEVI uint32_t idesc_bf16_m256(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
 }
 
 // 32 lanes x 32 consecutive fp32 columns from TMEM into registers (lane = accumulator row).

@@ -15,6 +15,7 @@
 
 #include <float.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 #include <queue>
 #include <type_traits>
@@ -493,9 +494,10 @@ __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn,
   // SYRK tiles on the diagonal: for this warp's 32 rows the chunks left of column row0 hold no direct or mirrored
   // element (every offset is a multiple of 32), the chunk starting at row0 is masked per element (MASK), and the
   // chunks to its right are above the diagonal.
-  const int c_first = DG ? (int)(row0 - n0) : 0;
+  // (In a 256-row pair tile the second CTA's rows can lie wholly below the diagonal: c_first >= bn.)
+  const int c_first = DG ? (int)min(row0 - n0, (long long)bn) : 0;
   float4 pv[8];
-  if (pre_src) {
+  if (pre_src && c_first < bn) {
 #pragma unroll
     for (int it = 0; it < 8; ++it)
       pv[it] = *reinterpret_cast<const float4*>(pre_src + (row0 + rs + 4 * it) * pre_ld + n0 + c_first + 4 * cg);
@@ -674,7 +676,7 @@ __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn,
   };
 
   int c0 = c_first;
-  if (DG) {
+  if (DG && c0 < bn) {
     chunk(c0, std::integral_constant<bool, true>());
     c0 += 32;
   }
@@ -948,6 +950,226 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   gemm_body<SPLIT, BNMAX, STAGES, KIND>(&desc, tiles, ntiles, err);
 }
 
+// ---- the pair kernel (tcgen05 cta_group::2) ------------------------------------------------------------------------
+// A cluster of two CTAs on neighbouring SMs computes 256 x bn tiles: each CTA stages its 128 rows of A and its half
+// (bn / 2 rows) of B, the leader (cluster rank 0) issues M = 256 MMAs that read both CTAs' shared memory, and each
+// CTA's TMEM receives its 128 accumulator rows, which its own epilogue warps store. Per SM this halves the B
+// operand's shared-memory and L2 traffic against the one-CTA kernel. Handshakes (all waits bounded):
+//   full[s]  (leader)   both CTAs' TMA copies of stage s land here (cta_group::2 copies signal the leader's barrier);
+//                       the leader's producer sets the expected bytes of both CTAs;
+//   go[s]    (peer)     the leader's producer arrives when it has armed full[s] for the round, so the peer never
+//                       issues copies the leader does not count (on abort the leader drains every armed round);
+//   empty[s] (both)     the leader's MMA commit, multicast to both CTAs, frees stage s;
+//   tfull[a] (both)     the leader's commit, multicast, hands accumulator a to both epilogues;
+//   tempty[a] (leader)  four epilogue warps of each CTA arrive (the peer's remotely) when accumulator a is drained.
+template <int BNMAX, int STAGES>
+struct PairCfg {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = (BNMAX / 2) * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int TMEM_COLS = 2 * BNMAX;
+  static constexpr int CTRL_BYTES = 512;
+  static constexpr int RED_FLOATS = 4 * BNMAX + BNMAX + 32 + 4 * 32 * 36;
+  static constexpr int SMEM_BYTES = 1024 + TILE_BYTES + CTRL_BYTES + RED_FLOATS * 4;
+  static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
+  static_assert((3 * STAGES + 5) * 8 + 8 <= CTRL_BYTES, "barriers must fit the control block");
+};
+constexpr int PBM = 2 * BM;  // rows of a pair tile
+
+template <int BNMAX, int STAGES, int KIND>
+__device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ descs, const uint32_t* __restrict__ tiles,
+                                               int* err) {
+  using C = PairCfg<BNMAX, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::TILE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* go = empty + STAGES;
+  uint64_t* tfull = go + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* red = reinterpret_cast<float*>(smem + C::TILE_BYTES + C::CTRL_BYTES);
+  float* cs = red + 4 * BNMAX;
+  float* misc = cs + BNMAX;
+  volatile int* epi_ok = reinterpret_cast<volatile int*>(misc + 16);
+  float* stage_all = misc + 32;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();  // 0: leader
+  // This cluster's segment of the tile list.
+  const int nseg = (int)tiles[0], cl = (int)(blockIdx.x >> 1);
+  const int t_begin = cl < nseg ? (int)tiles[1 + cl] : 0;
+  const int t_end = cl < nseg ? (int)tiles[2 + cl] : 0;
+  tiles += 2 * tile_header_pairs(nseg);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&go[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);
+    }
+    mbar_init(drain, 1);
+    *abort = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before any remote arrive or copy signal
+  if (warp == 1) {
+    __syncwarp();
+    tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs) ----------------
+      uint32_t g = 0;
+      uint32_t armed[STAGES];  // rounds the leader armed per stage, drained on abort
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) armed[s] = 0;
+      for (int t = t_begin; t < t_end && !*abort; ++t) {
+        int p, tm, tn;
+        get_tile(descs, tiles, t, p, tm, tn);
+        const GemmDesc& d = descs[p];
+        const int nk = (d.s.K + BK - 1) / BK;
+        const int half = d.s.bn / 2;
+        const uint32_t bytes = 2u * (uint32_t)(C::A_BYTES + half * BK * 2);  // both CTAs' copies
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % STAGES;
+          const uint32_t ph = (g / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort)) break;
+          if (rank == 0) {
+            mbar_arrive_expect_tx(&full[s], bytes);
+            armed[s] += 1;
+            mbar_arrive_cluster_relaxed(mapa_shared(&go[s], 1));
+          } else if (!mbar_wait(&go[s], ph, abort)) {
+            break;
+          }
+          uint8_t* sa = smem + s * C::STAGE_BYTES;
+          const uint32_t fb = mapa_shared(&full[s], 0);
+          tma_load_2d_pair(sa, &d.ta[0], fb, kb * BK, tm * PBM + (int)rank * BM);
+          tma_load_2d_pair(sa + C::A_BYTES, &d.tb[0], fb, kb * BK, tn * d.s.bn + (int)rank * half);
+        }
+      }
+      if (*abort && rank == 0) {  // every armed round (both CTAs' copies) lands before shared memory is released
+        for (int s = 0; s < STAGES; ++s) {
+          if (armed[s] == 0) continue;
+          volatile int never = 0;
+          mbar_wait(&full[s], (armed[s] - 1) & 1, &never);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer (leader) ----------------
+      uint32_t g = 0, i = 0;
+      bool issued = false;
+      for (int t = t_begin; t < t_end; ++t, ++i) {
+        int p, tm, tn;
+        get_tile(descs, tiles, t, p, tm, tn);
+        const GemmDesc& d = descs[p];
+        const int nk = (d.s.K + BK - 1) / BK;
+        const uint32_t acc = i & 1, aph = (i >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], aph ^ 1, abort)) break;
+        tc_fence_after();
+        const uint32_t dt = tmem_base + acc * BNMAX;
+        const uint32_t idesc = idesc_bf16_m256(d.s.bn);
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % STAGES;
+          const uint32_t ph = (g / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + s * C::STAGE_BYTES);
+          const uint32_t b0 = a0 + C::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_bf16_pair(dt, sdesc_k_sw128(a0 + kk * 32), sdesc_k_sw128(b0 + kk * 32), idesc, (kb | kk) != 0);
+          issued = true;
+          umma_commit_pair(&empty[s], 3);
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[acc], 3);
+      }
+      if (*abort && issued) {  // every issued MMA (it reads both CTAs' shared memory) finishes first
+        umma_commit_pair(drain, 1);
+        volatile int never = 0;
+        mbar_wait(drain, 0, &never);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
+    const int q = warp & 3;
+    const uint32_t tempty_leader0 = mapa_shared(&tempty[0], 0), tempty_leader1 = mapa_shared(&tempty[1], 0);
+    uint32_t i = 0;
+    for (int t = t_begin; t < t_end; ++t, ++i) {
+      int p, tm, tn;
+      get_tile(descs, tiles, t, p, tm, tn);
+      const GemmDesc& d = descs[p];
+      const int tm128 = 2 * tm + (int)rank;  // this CTA's 128 rows of the pair tile
+      const uint32_t acc = i & 1, aph = (i >> 1) & 1;
+      const bool ok = mbar_wait(&tfull[acc], aph, abort);
+      if (lane == 0) epi_ok[q] = ok ? 1 : 0;
+      named_sync(1, 128);
+      const bool all_ok = epi_ok[0] && epi_ok[1] && epi_ok[2] && epi_ok[3];
+      named_sync(1, 128);
+      if (!all_ok) break;
+      tc_fence_after();
+      const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BNMAX;
+      float* stg = stage_all + q * 32 * STG;
+      const long long m0 = (long long)tm128 * BM, n0 = (long long)tn * d.s.bn;
+      if (m0 < d.s.M) {
+        const bool interior = m0 + BM <= d.s.M && n0 + d.s.bn <= d.s.N;
+        const bool fast = KIND != EPI_GENERIC && d.fast == KIND && interior;
+        if constexpr (KIND == EPI_SYRK) {
+          if (fast && n0 >= m0 + BM) epilogue_fast<KIND, BNMAX, false>(d, tm128, tn, tacc, q, lane, red, cs, misc, stg);
+          else if (fast) epilogue_fast<KIND, BNMAX, true>(d, tm128, tn, tacc, q, lane, red, cs, misc, stg);
+          else epilogue_tile<BNMAX>(d, tm128, tn, tacc, q, lane, red, cs, misc, stg);
+        } else {
+          if (fast) epilogue_fast<KIND, BNMAX, false>(d, tm128, tn, tacc, q, lane, red, cs, misc, stg);
+          else epilogue_tile<BNMAX>(d, tm128, tn, tacc, q, lane, red, cs, misc, stg);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0) mbar_arrive(&tempty[acc]);
+        else mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA releases shared memory or TMEM while the other may still use them
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+  }
+  if (threadIdx.x == 0 && *abort) atomicOr(err, ERR_TIMEOUT_FULL);
+}
+
+template <int BNMAX, int STAGES, int KIND>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
+    gemm_pair_kernel(const GemmDesc* __restrict__ descs, const uint32_t* __restrict__ tiles, int* err) {
+  gemm_pair_body<BNMAX, STAGES, KIND>(descs, tiles, err);
+}
+
 // ---- host side --------------------------------------------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -1021,7 +1243,8 @@ static int fast_kind(const PsgdGemmSpec& s) {
   return EPI_PLAIN;
 }
 
-static int fill_desc(GemmDesc* d, const PsgdGemmSpec& s, int split) {
+// pair: the B map's box is the half of a tile's bn rows that each CTA of a pair stages.
+static int fill_desc(GemmDesc* d, const PsgdGemmSpec& s, int split, bool pair = false) {
   int rc = check_spec(s, split);
   if (rc) return rc;
   memset(d, 0, sizeof(GemmDesc));
@@ -1030,7 +1253,7 @@ static int fill_desc(GemmDesc* d, const PsgdGemmSpec& s, int split) {
   d->tiles_n = (s.N + s.bn - 1) / s.bn;
   d->fast = fast_kind(s);
   if ((rc = encode_bf16(&d->ta[0], s.a_hi, s.M, s.K, s.lda, BM))) return rc;
-  if ((rc = encode_bf16(&d->tb[0], s.b_hi, s.N, s.K, s.ldb, s.bn))) return rc;
+  if ((rc = encode_bf16(&d->tb[0], s.b_hi, s.N, s.K, s.ldb, pair ? s.bn / 2 : s.bn))) return rc;
   if (split != 1) {
     if ((rc = encode_bf16(&d->ta[1], s.a_lo, s.M, s.K, s.lda, BM))) return rc;
     if ((rc = encode_bf16(&d->tb[1], s.b_lo, s.N, s.K, s.ldb, s.bn))) return rc;
@@ -1041,23 +1264,32 @@ static int fill_desc(GemmDesc* d, const PsgdGemmSpec& s, int split) {
   return PSGD_OK;
 }
 
-static int spec_tiles(const PsgdGemmSpec& s) {
-  const int tmn = (s.M + BM - 1) / BM, tnn = (s.N + s.bn - 1) / s.bn;
+// Tiles of one problem, rows of height bm (BM for one CTA, PBM for a pair); SYRK: upper tiles only.
+static int spec_tiles(const PsgdGemmSpec& s, int bm = BM) {
+  const int tmn = (s.M + bm - 1) / bm, tnn = (s.N + s.bn - 1) / s.bn;
   if (s.mode == PSGD_GEMM_SYRK) {
     int n = 0;
-    for (int tm = 0; tm < tmn; ++tm) n += tnn - tm * BM / s.bn;
+    for (int tm = 0; tm < tmn; ++tm) n += tnn - tm * bm / s.bn;
     return n;
   }
   return tmn * tnn;
 }
 
-static void append_tiles(const PsgdGemmSpec& s, uint32_t p, uint32_t* out, int& k) {
-  const int tmn = (s.M + BM - 1) / BM, tnn = (s.N + s.bn - 1) / s.bn;
-  for (int tm = 0; tm < tmn; ++tm)
-    for (int tn = (s.mode == PSGD_GEMM_SYRK ? tm * BM / s.bn : 0); tn < tnn; ++tn) {
-      out[2 * k] = p;
-      out[2 * k + 1] = ((uint32_t)tm << 16) | (uint32_t)tn;
-      ++k;
+// Tile order of one problem: blocks of RASTER_W tile columns, each walked row by row, so the tiles that run at the
+// same time (neighbours in this order) share a few B panels and a band of A panels that stay resident in L2.
+constexpr int RASTER_W = 8;
+
+static void append_tiles(const PsgdGemmSpec& s, uint32_t p, uint32_t* out, int& k, int bm = BM) {
+  const int tmn = (s.M + bm - 1) / bm, tnn = (s.N + s.bn - 1) / s.bn;
+  const bool syrk = s.mode == PSGD_GEMM_SYRK;
+  for (int c0 = 0; c0 < tnn; c0 += RASTER_W)
+    for (int tm = 0; tm < tmn; ++tm) {
+      const int lo = syrk ? max(c0, tm * bm / s.bn) : c0;
+      for (int tn = lo; tn < min(c0 + RASTER_W, tnn); ++tn) {
+        out[2 * k] = p;
+        out[2 * k + 1] = ((uint32_t)tm << 16) | (uint32_t)tn;
+        ++k;
+      }
     }
 }
 
@@ -1071,13 +1303,13 @@ static int num_sms() {
 
 // Raises the dynamic shared-memory limit of a kernel once per device (never inside a graph capture afterwards).
 static bool smem_attr_once(const void* fn, int bytes) {
-  static const void* done[64][8] = {};  // per device: kernels already configured
+  static const void* done[64][32] = {};  // per device: kernels already configured
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < 32; ++i)
     if (done[dev][i] == fn) return true;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < 32; ++i)
     if (done[dev][i] == nullptr) {
       done[dev][i] = fn;
       break;
@@ -1103,6 +1335,88 @@ static int launch_single(const GemmDesc& desc, const uint32_t* tiles, int ntiles
   const int grid = ntiles < num_sms() ? ntiles : num_sms();
   k<<<grid, GEMM_THREADS, C::SMEM_BYTES, st>>>(desc, tiles, ntiles, err);
   return cudaGetLastError() == cudaSuccess ? PSGD_OK : PSGD_ELAUNCH;
+}
+
+// ---- pair kernel launch: one cluster of two CTAs per segment of the tile list ----
+constexpr int PAIR_BN = 256, PAIR_STAGES = 6;
+constexpr int KIND_PAIR = 8;  // flag in the encoded kind: the group runs on the pair kernel
+
+// Clusters a pair launch uses on the current device: as many as can be resident at once (at most SMs / 2).
+static int pair_clusters() {
+  static int cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return num_sms() / 2;
+  if (cached[dev] > 0) return cached[dev];
+  using C = PairCfg<PAIR_BN, PAIR_STAGES>;
+  auto k = gemm_pair_kernel<PAIR_BN, PAIR_STAGES, EPI_GENERIC>;
+  int n = num_sms() / 2;
+  if (smem_attr_once(reinterpret_cast<const void*>(k), C::SMEM_BYTES)) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * n);
+    cfg.blockDim = dim3(GEMM_THREADS);
+    cfg.dynamicSmemBytes = C::SMEM_BYTES;
+    cudaLaunchAttribute at;
+    at.id = cudaLaunchAttributeClusterDimension;
+    at.val.clusterDim.x = 2;
+    at.val.clusterDim.y = 1;
+    at.val.clusterDim.z = 1;
+    cfg.attrs = &at;
+    cfg.numAttrs = 1;
+    int active = 0;
+    if (cudaOccupancyMaxActiveClusters(&active, reinterpret_cast<const void*>(k), &cfg) == cudaSuccess && active > 0 &&
+        active < n)
+      n = active;
+  }
+  cached[dev] = n;
+  return n;
+}
+
+template <int KIND>
+static int launch_pair(const GemmDesc* descs, const uint32_t* tiles, int* err, cudaStream_t st) {
+  using C = PairCfg<PAIR_BN, PAIR_STAGES>;
+  auto k = gemm_pair_kernel<PAIR_BN, PAIR_STAGES, KIND>;
+  if (!smem_attr_once(reinterpret_cast<const void*>(k), C::SMEM_BYTES)) return PSGD_ELAUNCH;
+  k<<<2 * pair_clusters(), GEMM_THREADS, C::SMEM_BYTES, st>>>(descs, tiles, err);
+  return cudaGetLastError() == cudaSuccess ? PSGD_OK : PSGD_ELAUNCH;
+}
+
+static int launch_pair_kind(const GemmDesc* d, const uint32_t* tiles, int kind, int* err, cudaStream_t st) {
+  switch (kind) {
+    case EPI_AUX: return launch_pair<EPI_AUX>(d, tiles, err, st);
+    case EPI_NLB: return launch_pair<EPI_NLB>(d, tiles, err, st);
+    case EPI_PLAIN: return launch_pair<EPI_PLAIN>(d, tiles, err, st);
+    case EPI_SYRK: return launch_pair<EPI_SYRK>(d, tiles, err, st);
+    default: return launch_pair<EPI_GENERIC>(d, tiles, err, st);
+  }
+}
+
+// A group runs on the pair kernel when every problem is one-MMA (bf16, no lo operands), its tiles are 128 or 256
+// columns wide, neither CTA of a pair tile ever stages a wholly out-of-range box (rows past the last full 128-row
+// half, columns past the last bn/2 half), and its reductions are long. PSGD_GEMM_PAIR=0 in the environment keeps
+// every group on the one-CTA kernel; PSGD_GEMM_PAIR=1 drops the length rule.
+static bool pair_eligible(const PsgdGemmSpec* specs, int nspecs) {
+  const char* env = getenv("PSGD_GEMM_PAIR");
+  if (env && env[0] == '0') return false;
+  // Pairs pay off on long reductions (measured: up to +9% at K >= 4096, -8% at K = 1024, where the epilogue bounds
+  // the tile): the group's flop-weighted K decides unless PSGD_GEMM_PAIR=1 forces pairs.
+  if (!(env && env[0] == '1')) {
+    double fl = 0.0, flk = 0.0;
+    for (int i = 0; i < nspecs; ++i) {
+      const double f = (double)specs[i].M * specs[i].N * specs[i].K;
+      fl += f;
+      flk += f * specs[i].K;
+    }
+    if (fl <= 0.0 || flk / fl < 2048.0) return false;
+  }
+  for (int i = 0; i < nspecs; ++i) {
+    const PsgdGemmSpec& s = specs[i];
+    if (s.a_lo || s.b_lo) return false;
+    if (s.bn != 128 && s.bn != 256) return false;
+    const int rm = s.M % PBM, rn = s.N % s.bn;
+    if (rm != 0 && rm <= BM) return false;
+    if (rn != 0 && rn <= s.bn / 2) return false;
+  }
+  return true;
 }
 
 template <int SPLIT, int BNMAX, int STAGES>
@@ -1149,12 +1463,12 @@ extern "C" int psgd_gemm_count_tiles(const PsgdGemmSpec* specs, int nspecs) {
 // Estimated cycles a tile holds its CTA: the slower of its MMAs (one 128 x 256 x 64 block step ~730 cycles at the
 // tensor-core rate, three MMAs per step in split mode) and its epilogue (per 32-column chunk; the general epilogue
 // is several times dearer than the specialised ones). The accumulators are double-buffered, so the two overlap.
-static double tile_cost(const GemmDesc& d, int tm, int tn, int kind) {
+static double tile_cost(const GemmDesc& d, int tm, int tn, int kind, int bm) {
   const PsgdGemmSpec& s = d.s;
   const double nk = (double)((s.K + BK - 1) / BK);
   const double mma = nk * 730.0 * (s.bn / 256.0) * ((s.a_lo && s.b_lo) ? 3.0 : 1.0) + 1500.0;
-  const long long m0 = (long long)tm * BM, n0 = (long long)tn * s.bn;
-  const bool interior = m0 + BM <= s.M && n0 + s.bn <= s.N;
+  const long long m0 = (long long)tm * bm, n0 = (long long)tn * s.bn;
+  const bool interior = m0 + bm <= s.M && n0 + s.bn <= s.N;
   const bool fast = kind != EPI_GENERIC && d.fast == kind && interior;
   const double epi = (s.bn / 32.0) * (fast ? 3000.0 : 12000.0);
   return mma > epi ? mma : epi;
@@ -1169,31 +1483,33 @@ extern "C" int psgd_gemm_encode(const PsgdGemmSpec* specs, int nspecs, void* hos
   if (need < 0) return need;
   if (need > max_tiles) return PSGD_ESPACE;
   GemmDesc* descs = reinterpret_cast<GemmDesc*>(host_table);
+  const bool pair = pair_eligible(specs, nspecs);
+  const int bm = pair ? PBM : BM;
   // split is a launch-time choice; encode the lo maps whenever lo pointers are present
   for (int i = 0; i < nspecs; ++i) {
     const int split = (specs[i].a_lo && specs[i].b_lo) ? 3 : 1;
-    const int rc = fill_desc(&descs[i], specs[i], split == 3 && specs[i].bn > 128 ? 1 : split);
+    const int rc = fill_desc(&descs[i], specs[i], split == 3 && specs[i].bn > 128 ? 1 : split, pair);
     if (rc) return rc;
   }
   // the group's epilogue kind: the fast kind covering the most tiles (its problems take the fast path)
   long long w[5] = {0, 0, 0, 0, 0};
-  for (int i = 0; i < nspecs; ++i) w[descs[i].fast] += spec_tiles(specs[i]);
+  for (int i = 0; i < nspecs; ++i) w[descs[i].fast] += spec_tiles(specs[i], bm);
   int best = EPI_GENERIC;
   for (int t = 1; t < 5; ++t)
     if (w[t] > w[best] || (best == EPI_GENERIC && w[t] > 0)) best = t;
-  *kind = best;
+  *kind = best | (pair ? KIND_PAIR : 0);
 
   // Tiles in their natural order (problems as given, row-major within each), each handed to the CTA with the
   // least estimated work so far: neighbouring tiles (which share operand panels in L2) run at about the same
   // time, and costly tiles (long K, the general epilogue) do not pile up on a few CTAs.
-  const int nseg = num_sms();
+  const int nseg = pair ? pair_clusters() : num_sms();  // one segment per CTA, or per pair of CTAs
   const int hdr = tile_header_pairs(nseg);
   std::vector<uint32_t> all;
   all.reserve(2 * (size_t)(need - hdr));
   for (int i = 0; i < nspecs; ++i) {
     int k = 0;
-    std::vector<uint32_t> one(2 * (size_t)spec_tiles(specs[i]));
-    append_tiles(specs[i], (uint32_t)i, one.data(), k);
+    std::vector<uint32_t> one(2 * (size_t)spec_tiles(specs[i], bm));
+    append_tiles(specs[i], (uint32_t)i, one.data(), k, bm);
     all.insert(all.end(), one.begin(), one.end());
   }
   const int nt = (int)(all.size() / 2);
@@ -1207,7 +1523,7 @@ extern "C" int psgd_gemm_encode(const PsgdGemmSpec* specs, int nspecs, void* hos
     const int p = (int)all[2 * t], tm = (int)(all[2 * t + 1] >> 16), tn = (int)(all[2 * t + 1] & 0xFFFF);
     owner[t] = top.second;
     count[top.second] += 1;
-    pq.push({top.first + tile_cost(descs[p], tm, tn, best), top.second});
+    pq.push({top.first + tile_cost(descs[p], tm, tn, best, bm), top.second});
   }
   uint32_t* h = host_tiles;  // header: nseg, then nseg + 1 offsets
   h[0] = (uint32_t)nseg;
@@ -1227,9 +1543,11 @@ extern "C" int psgd_gemm_encode(const PsgdGemmSpec* specs, int nspecs, void* hos
 
 extern "C" int psgd_gemm_launch(const void* dev_table, const uint32_t* dev_tiles, int ntiles, int split, int kind,
                                 int* dev_err, cudaStream_t stream) {
-  if (!dev_table || !dev_tiles || ntiles < 0 || !dev_err || kind < 0 || kind > 4) return PSGD_EINVAL;
+  if (!dev_table || !dev_tiles || ntiles < 0 || !dev_err || kind < 0 || (kind & 7) > 4 || kind > (KIND_PAIR | 4))
+    return PSGD_EINVAL;
   if (ntiles == 0) return PSGD_OK;
   const GemmDesc* d = reinterpret_cast<const GemmDesc*>(dev_table);
+  if (kind & KIND_PAIR) return split == 1 ? launch_pair_kind(d, dev_tiles, kind & 7, dev_err, stream) : PSGD_EINVAL;
   if (split == 1) return launch_group_kind<1, 256, 4>(d, dev_tiles, ntiles, kind, dev_err, stream);
   if (split == 3) return launch_group_kind<3, 128, 3>(d, dev_tiles, ntiles, kind, dev_err, stream);
   return PSGD_EINVAL;

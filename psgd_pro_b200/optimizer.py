@@ -264,7 +264,7 @@ class _Plan:
         self.prep_a_work, self.prep_a_n = _work(pa, dev)
 
         # U1, U2: Pg of the noisy gradient
-        u1, u2, u3 = [], [], []
+        u1, u2, u3, u3r = [], [], [], []
         for p in P:
             n1, n2, f1, f2 = p.n1, p.n2, p.f1, p.f2
             if p.kind == ("dense", "dense"):
@@ -294,8 +294,9 @@ class _Plan:
                 u3.append(self.syrk(p.pgT, n2, n1, out_hi=f2.T[0], out_lo=f2.T[1], part_row=f2.t_rows,
                                     diag_out=f2.t_diag))
             if f2.kind == "dense" and f2.rank1:
-                u3.append(self.spec(f2.qta, p.pg_op, n2, 1, n2, bn=16, out_hi=p.w[0], out_lo=p.w[1]))
-        self.g_u1, self.g_u2, self.g_u3 = self.group(u1), self.group(u2), self.group(u3)
+                u3r.append(self.spec(f2.qta, p.pg_op, n2, 1, n2, bn=16, out_hi=p.w[0], out_lo=p.w[1]))
+        # the skinny rank-one products form groups of their own, so the big products' groups can run on CTA pairs
+        self.g_u1, self.g_u2, self.g_u3, self.g_u3r = self.group(u1), self.group(u2), self.group(u3), self.group(u3r)
 
         dense = [f for f in self.factors if f.kind == "dense"]
         nlb = [f for f in dense if not f.rank1]
@@ -321,16 +322,16 @@ class _Plan:
             fi.append(it)
         self.fac_dev, self.fac_n = _upload(_capi.FactorItem, fi, dev), len(fi)
         # U10: q <- q - lr/L (term1 q - term2 q)
-        u10 = []
+        u10, u10r = [], []
         for f in dense:
             kw = dict(alpha_ptr=self.s(f, S_AQ), beta_ptr=self.s(f, S_BQ), alpha=1.0, beta=1.0, aux=f.q,
                       out_f32=f.q, out_hi_t=f.qtb[0], out_lo_t=f.qtb[1])
             if f.rank1:
                 p = next(p for p in P if p.f2 is f)
-                u10.append(self.spec(p.pgT, p.w, f.n, f.n, 1, **kw))
+                u10r.append(self.spec(p.pgT, p.w, f.n, f.n, 1, **kw))
             else:
                 u10.append(self.spec(f.T, f.qta, f.n, f.n, f.n, **kw))
-        self.g_u10 = self.group(u10)
+        self.g_u10, self.g_u10r = self.group(u10), self.group(u10r)
         # U11: Rn = Q - Q^T
         sk, skw = [], []
         for f in dense:
@@ -507,6 +508,8 @@ class _Plan:
         tr("u2")
         self._launch(self.g_u3)
         tr("term1")
+        self._launch(self.g_u3r)
+        tr("term1_r1")
         check(L.psgd_nlb_prep(self.nlb_spd_dev.data_ptr(), self.nlb_spd_n, err, st), "nlb_prep spd")
         tr("nlb_prep_spd")
         for k, g in enumerate(self.g_spd):
@@ -516,6 +519,8 @@ class _Plan:
         tr("factor")
         self._launch(self.g_u10)
         tr("qupdate")
+        self._launch(self.g_u10r)
+        tr("qupdate_r1")
         check(L.psgd_skew(self.skew_dev.data_ptr(), self.skew_work.data_ptr(), self.skew_n, err, st), "skew")
         tr("skew")
         check(L.psgd_nlb_prep(self.nlb_skh_dev.data_ptr(), self.nlb_skh_n, err, st), "nlb_prep skh")
@@ -549,9 +554,9 @@ class _Plan:
 
     def phase_groups(self):
         """(name, GemmGroup) of every tensor-core phase, in the names run_update / run_apply trace."""
-        out = [("u1", self.g_u1), ("u2", self.g_u2), ("term1", self.g_u3)]
+        out = [("u1", self.g_u1), ("u2", self.g_u2), ("term1", self.g_u3), ("term1_r1", self.g_u3r)]
         out += [(f"nlb_spd{k}", g) for k, g in enumerate(self.g_spd)]
-        out += [("qupdate", self.g_u10)]
+        out += [("qupdate", self.g_u10), ("qupdate_r1", self.g_u10r)]
         out += [(f"nlb_skh{k}", g) for k, g in enumerate(self.g_skh)]
         out += [("S", self.g_u17), ("procrustes", self.g_u20), ("gram", self.g_u22), ("a1", self.g_a1),
                 ("a2", self.g_a2)]
@@ -564,7 +569,8 @@ class _Plan:
         if update:
             n += 1 + 2 * int(self.nlb_spd_n > 0) + 2 + 2 * int(self.skew_n > 0)  # prep, nlb preps, factor x2, skew, rot
             n -= int(self.skf_n == 0)
-            groups += [self.g_u1, self.g_u2, self.g_u3, self.g_u10, self.g_u17, self.g_u20, self.g_u22]
+            groups += [self.g_u1, self.g_u2, self.g_u3, self.g_u3r, self.g_u10, self.g_u10r, self.g_u17, self.g_u20,
+                       self.g_u22]
             groups += self.g_spd + self.g_skh
         return n + sum(g is not None for g in groups)
 

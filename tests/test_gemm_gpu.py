@@ -168,3 +168,100 @@ def test_group_launch(cuda, split):
     assert err.item() == 0
     for o, r in zip(outs, refs):
         assert rel(o, r) < (2e-5 if split == 3 else 1e-5)
+
+
+def _pair_group(cuda, build, pair, monkeypatch):
+    """The same problems encoded for the pair kernel (tcgen05 cta_group::2) or, with PSGD_GEMM_PAIR=0, for the
+    one-CTA kernel; returns the outputs after two launches."""
+    monkeypatch.setenv("PSGD_GEMM_PAIR", "1" if pair else "0")
+    specs, outs, keep = build()
+    grp = K.GemmGroup(specs, 1, cuda, keep=keep)
+    assert bool(grp.kind & 8) == pair
+    err = err_word(cuda)
+    grp.launch(err)
+    grp.launch(err)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    return outs
+
+
+def test_pair_kernel_plain_and_transposed(cuda, monkeypatch):
+    g = torch.Generator().manual_seed(23)
+    shapes = [(512, 512, 320, 256), (768, 1024, 200, 256), (256, 256, 64, 256), (768, 384, 128, 128),
+              (1280, 2560, 1000, 256), (400, 400, 77, 256)]  # the last one: partial pair tiles on both edges
+    data = [(bf16_operand(M, Kd, cuda, g), bf16_operand(N, Kd, cuda, g)) for (M, N, Kd, bn) in shapes]
+
+    def build():
+        specs, outs, keep = [], [], []
+        for (M, N, Kd, bn), ((a, A), (b, B)) in zip(shapes, data):
+            out = torch.full((M, N), float("nan"), device=cuda)
+            ht = K.operand(N, M, cuda, split=False)
+            keep += [A, B, ht]
+            specs.append(K.make_spec(A, B, M, N, Kd, bn=bn, out_f32=out, out_hi_t=ht[0]))
+            outs.append((out, ht[0]))
+        return specs, outs, keep
+
+    pair = _pair_group(cuda, build, True, monkeypatch)
+    single = _pair_group(cuda, build, False, monkeypatch)
+    for (M, N, Kd, bn), ((a, A), (b, B)), (o, t), (o1, t1) in zip(shapes, data, pair, single):
+        ref = A[0][:, :Kd].double() @ B[0][:, :Kd].double().T
+        assert rel(o, ref) < 1e-5, (M, N)
+        assert rel(o, o1) < 1e-6
+        assert rel(t[:, :M].float(), ref.T) < 1e-2
+
+
+def test_pair_kernel_syrk_reductions(cuda, monkeypatch):
+    g = torch.Generator().manual_seed(29)
+    cases = [(512, 96), (768, 300), (1280, 64), (2048, 512)]
+    data = [bf16_operand(n, Kd, cuda, g) for n, Kd in cases]
+    qs = [torch.randn(n, n, generator=g).to(cuda) for n, _ in cases]
+
+    def build():
+        specs, outs, keep = [], [], []
+        for (n, Kd), (x, X), q in zip(cases, data, qs):
+            Tm, Tn = (n + 127) // 128, (n + 255) // 256
+            out = torch.full((n, n), float("nan"), device=cuda)
+            hi = K.operand(n, n, cuda, split=False)
+            part_row = torch.zeros(Tn + Tm, n, device=cuda)
+            diag = torch.empty(n, device=cuda)
+            part_dot = torch.zeros(Tm * Tn, device=cuda)
+            keep += [X, hi]
+            specs.append(K.make_spec(X, X, n, n, Kd, bn=256, mode=K.PSGD_GEMM_SYRK, out_f32=out, out_hi=hi[0],
+                                     part_row=part_row, diag_out=diag, dot_aux=q, part_dot=part_dot))
+            outs.append((out, part_row, diag, part_dot))
+        return specs, outs, keep
+
+    for pair in (True, False):
+        for (n, Kd), (x, X), q, (out, part_row, diag, part_dot) in zip(cases, data, qs,
+                                                                      _pair_group(cuda, build, pair, monkeypatch)):
+            ref = X[0][:, :Kd].double() @ X[0][:, :Kd].double().T
+            assert torch.equal(out, out.T), (n, pair)
+            assert rel(out, ref) < 1e-5
+            assert rel(part_row.sum(0), (ref ** 2).sum(1)) < 1e-4
+            assert rel(diag, ref.diagonal()) < 2e-5
+            want = (ref * q.double()).sum().item()
+            assert abs(part_dot.double().sum().item() - want) <= 1e-4 * (ref.abs() * q.double().abs()).sum().item()
+
+
+def test_pair_kernel_aux_epilogue(cuda, monkeypatch):
+    """The q-update form: Q <- beta Q + alpha (A B^T) with device scalars, Q^T stored as bf16."""
+    g = torch.Generator().manual_seed(31)
+    n = 1024
+    (a, A), (b, B) = bf16_operand(n, n, cuda, g), bf16_operand(n, n, cuda, g, scale=0.01)
+    q0 = torch.randn(n, n, generator=g).to(cuda)
+    alpha = torch.tensor([-0.05], device=cuda)
+
+    def build():
+        q = q0.clone()
+        qt = K.operand(n, n, cuda, split=False)
+        spec = K.make_spec(A, B, n, n, n, bn=256, alpha_ptr=alpha, alpha=1.0, beta=1.0, aux=q, out_f32=q,
+                           out_hi_t=qt[0])
+        return [spec], [(q, qt[0])], [A, B, qt, q]
+
+    (q, qt), = _pair_group(cuda, build, True, monkeypatch)
+    (q1, _), = _pair_group(cuda, build, False, monkeypatch)
+    step = A[0][:, :n].double() @ B[0][:, :n].double().T
+    ref = q0.double() + 2 * (-0.05) * step  # two launches, the second on the first's output
+    assert rel(q, ref) < 1e-5
+    assert rel(q, q1) < 1e-6
+    assert rel(qt[:, :n].float(), q.T) < 1e-2
