@@ -108,7 +108,10 @@ int psgd_num_sms(void);
 #define PSGD_HY_MAX_AVG 4      /* grad_clip_max_amps[0] */
 #define PSGD_HY_MAX_ELEM 5     /* grad_clip_max_amps[1] */
 #define PSGD_HY_MOM_BETA 6     /* momentum factor of this step */
-#define PSGD_HY_COUNT 8
+#define PSGD_HY_NOISE 7        /* nonzero: psgd_prep generates the damping noise itself (below) */
+#define PSGD_HY_NOISE_KEY0 8   /* the generator's key, two uint32 stored bit for bit in float slots */
+#define PSGD_HY_NOISE_KEY1 9
+#define PSGD_HY_COUNT 12
 
 /* Gradient staging on 32 x 32 tiles of an n1 x n2 gradient G (fp32 or bf16, contiguous):
  * x = G + (damping + eps |G|) * xi when xi != NULL (the damping noise of psgd_pro.py:122-123), else x = G.
@@ -120,6 +123,11 @@ int psgd_num_sms(void);
  * (ti << 16) | tj) 32 x 32 tiles otherwise. Replaces the exprP prologue of psgd_pro.py:123 and
  * psgd_pro_fast.py:176. */
 #define PSGD_PREP_ROWS 8   /* PREP_NORMAL work entries cover PSGD_PREP_ROWS rows: (item, row block) */
+/* Damping noise (items with xi != NULL): read from xi, or, when hyper[PSGD_HY_NOISE] != 0, generated in the kernel:
+ * element e (index i * n2 + j of the item) gets the standard normal number s = noise_base + e of the sequence
+ * Philox4x32-10 (Salmon et al., SC'11) with key (KEY0, KEY1) and counter (s / 4, 0, 0, 0), its four words taken as
+ * two Box-Muller pairs (words 0, 1 give numbers 4c, 4c + 1; words 2, 3 give 4c + 2, 4c + 3). The values depend on
+ * the key and position only, not on the launch geometry. */
 #define PSGD_PREP_NORMAL 0
 #define PSGD_PREP_TRANS 1
 #define PSGD_PREP_DIRECT 2
@@ -132,6 +140,7 @@ typedef struct PsgdPrepItem {
   float* out_f32;
   float* part_row; float* part_col; float* part_tile;
   float eps;
+  long long noise_base;  /* position of element 0 in the generated noise sequence (a multiple of 4) */
 } PsgdPrepItem;
 int psgd_prep(const PsgdPrepItem* items, const uint32_t* work, int nwork, const float* hyper, int* dev_err,
               cudaStream_t stream);

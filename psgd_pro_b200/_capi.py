@@ -41,7 +41,8 @@ class GemmSpec(ctypes.Structure):
 class PrepItem(ctypes.Structure):
     _fields_ = [("g", c_vp), ("g_bf16", c_int), ("mode", c_int), ("xi", c_vp), ("n1", c_int), ("n2", c_int),
                 ("p1", c_vp), ("p2", c_vp), ("out_hi", c_vp), ("out_lo", c_vp), ("ld_out", c_ll),
-                ("out_f32", c_vp), ("part_row", c_vp), ("part_col", c_vp), ("part_tile", c_vp), ("eps", c_float)]
+                ("out_f32", c_vp), ("part_row", c_vp), ("part_col", c_vp), ("part_tile", c_vp), ("eps", c_float),
+                ("noise_base", c_ll)]
 
 
 class NlbPrepItem(ctypes.Structure):
@@ -86,7 +87,8 @@ PREP_ROWS = 8
 ROT_ROWS = 8
 SKEW_TILE = 64
 PSGD_FACTOR_DENSE, PSGD_FACTOR_RANK1, PSGD_FACTOR_DIAG, PSGD_FACTOR_SKEW = 0, 1, 2, 3
-HY_LR_PRECOND, HY_BETA_L, HY_DAMPING, HY_LR_PARAMS, HY_MAX_AVG, HY_MAX_ELEM, HY_MOM_BETA, HY_COUNT = range(8)
+HY_LR_PRECOND, HY_BETA_L, HY_DAMPING, HY_LR_PARAMS, HY_MAX_AVG, HY_MAX_ELEM, HY_MOM_BETA = range(7)
+HY_NOISE, HY_NOISE_KEY0, HY_NOISE_KEY1, HY_COUNT = 7, 8, 9, 12
 APPLY_CHUNK = 8192
 
 # (name, restype, argtypes) of every exported entry point; tests check that each symbol is present.

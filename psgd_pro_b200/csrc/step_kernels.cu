@@ -32,6 +32,43 @@ PSGD_DEVI float load_split(const void* hi, const void* lo, long long idx) {
   return v;
 }
 
+// ---- counter-based normal numbers ----------------------------------------------------------------------------
+// Philox4x32-10 (Salmon, Moraes, Dror and Shaw, "Parallel random numbers: as easy as 1, 2, 3", SC'11): ten rounds of
+// two 32 x 32 -> 64-bit multiplications on a 4-word counter, the 2-word key bumped by Weyl constants between
+// rounds. The four output words become four standard normal numbers by two Box-Muller transforms.
+PSGD_DEVI uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {
+  constexpr uint32_t M0 = 0xD2511F53u, M1 = 0xCD9E8D57u, W0 = 0x9E3779B9u, W1 = 0xBB67AE85u;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t hi0 = __umulhi(M0, c.x), lo0 = M0 * c.x;
+    const uint32_t hi1 = __umulhi(M1, c.z), lo1 = M1 * c.z;
+    c = make_uint4(hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0);
+    k0 += W0;
+    k1 += W1;
+  }
+  return c;
+}
+
+// Numbers 4 blk .. 4 blk + 3 of the sequence with key (k0, k1).
+PSGD_DEVI float4 normal4(unsigned long long blk, uint32_t k0, uint32_t k1) {
+  const uint4 w = philox4x32_10(make_uint4((uint32_t)blk, (uint32_t)(blk >> 32), 0u, 0u), k0, k1);
+  constexpr float inv32 = 2.3283064365386963e-10f;  // 2^-32: uniforms (w + 1/2) / 2^32 in (0, 1)
+  const float u0 = ((float)w.x + 0.5f) * inv32, u1 = ((float)w.y + 0.5f) * inv32;
+  const float u2 = ((float)w.z + 0.5f) * inv32, u3 = ((float)w.w + 0.5f) * inv32;
+  const float r0 = sqrtf(-2.f * logf(u0)), r1 = sqrtf(-2.f * logf(u2));
+  float s0, c0, s1, c1;
+  sincospif(2.f * u1, &s0, &c0);
+  sincospif(2.f * u3, &s1, &c1);
+  return make_float4(r0 * c0, r0 * s0, r1 * c1, r1 * s1);
+}
+
+// Number s of the sequence.
+PSGD_DEVI float normal1(unsigned long long s, uint32_t k0, uint32_t k1) {
+  const float4 v = normal4(s >> 2, k0, k1);
+  const int i = (int)(s & 3);
+  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+
 // ---- gradient staging ------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) prep_kernel(const PsgdPrepItem* __restrict__ items,
                                                   const uint32_t* __restrict__ work, int nwork,
@@ -41,6 +78,8 @@ __global__ void __launch_bounds__(256) prep_kernel(const PsgdPrepItem* __restric
   __shared__ float tred[TROWS];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const float damping = hyper[PSGD_HY_DAMPING];
+  const bool gen = hyper[PSGD_HY_NOISE] != 0.f;  // noise from the counter-based generator instead of xi
+  const uint32_t k0 = __float_as_uint(hyper[PSGD_HY_NOISE_KEY0]), k1 = __float_as_uint(hyper[PSGD_HY_NOISE_KEY1]);
   for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
     const PsgdPrepItem& it = items[work[2 * w]];
     if (it.mode == PSGD_PREP_NORMAL) {  // rows PREP_ROWS * wv .. : 4-element vectors along each row
@@ -48,7 +87,8 @@ __global__ void __launch_bounds__(256) prep_kernel(const PsgdPrepItem* __restric
       const int rows = (int)min((long long)PREP_ROWS, it.n1 - r0);
       const bool vec = (it.n2 % 4) == 0 &&
                        ((reinterpret_cast<uintptr_t>(it.g) & (it.g_bf16 ? 7 : 15)) == 0) &&
-                       (it.xi == nullptr || (reinterpret_cast<uintptr_t>(it.xi) & 15) == 0);
+                       (it.xi == nullptr || (reinterpret_cast<uintptr_t>(it.xi) & 15) == 0) &&
+                       (it.noise_base & 3) == 0;
       if (vec) {
         const int nv = it.n2 / 4;
         for (int k = threadIdx.x; k < rows * nv; k += blockDim.x) {
@@ -65,7 +105,8 @@ __global__ void __launch_bounds__(256) prep_kernel(const PsgdPrepItem* __restric
             x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
           }
           if (it.xi) {
-            const float4 z = *reinterpret_cast<const float4*>(it.xi + idx);
+            const float4 z = gen ? normal4((unsigned long long)(it.noise_base + idx) >> 2, k0, k1)
+                                 : *reinterpret_cast<const float4*>(it.xi + idx);
             const float zz[4] = {z.x, z.y, z.z, z.w};
 #pragma unroll
             for (int i = 0; i < 4; ++i) x[i] += (damping + it.eps * fabsf(x[i])) * zz[i];
@@ -83,7 +124,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const PsgdPrepItem* __restric
           const long long row = r0 + k / it.n2, col = k % it.n2;
           const long long idx = row * it.n2 + col;
           float x = load_g(it.g, it.g_bf16, idx);
-          if (it.xi) x += (damping + it.eps * fabsf(x)) * it.xi[idx];
+          if (it.xi) x += (damping + it.eps * fabsf(x)) * (gen ? normal1(it.noise_base + idx, k0, k1) : it.xi[idx]);
           store_split(it.out_hi, it.out_lo, row * it.ld_out + col, x);
         }
       }
@@ -100,7 +141,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const PsgdPrepItem* __restric
       if (i < it.n1 && j < it.n2) {
         const long long idx = (long long)i * it.n2 + j;
         x = load_g(it.g, it.g_bf16, idx);
-        if (it.xi) x += (damping + it.eps * fabsf(x)) * it.xi[idx];
+        if (it.xi) x += (damping + it.eps * fabsf(x)) * (gen ? normal1(it.noise_base + idx, k0, k1) : it.xi[idx]);
       }
       vals[u] = x;
     }

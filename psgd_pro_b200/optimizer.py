@@ -22,6 +22,7 @@ psgd_pro.py:19-41 converges to on a rank-one matrix) and term1 q = Pg (q^T Pg)^T
 """
 import ctypes
 import math
+import struct
 
 import torch
 
@@ -29,7 +30,7 @@ from . import _capi
 from . import kernels as K
 from ._capi import (PSGD_FACTOR_DENSE, PSGD_FACTOR_DIAG, PSGD_FACTOR_RANK1, PSGD_FACTOR_SKEW, PSGD_PREP_DIRECT,
                     PSGD_PREP_NORMAL, PSGD_PREP_TRANS, HY_COUNT, HY_LR_PRECOND, HY_BETA_L, HY_DAMPING, HY_LR_PARAMS,
-                    HY_MAX_AVG, HY_MAX_ELEM, HY_MOM_BETA, APPLY_CHUNK, check)
+                    HY_MAX_AVG, HY_MAX_ELEM, HY_MOM_BETA, HY_NOISE, HY_NOISE_KEY0, HY_NOISE_KEY1, APPLY_CHUNK, check)
 
 K_SUB = 32  # subspace dimension of the norm lower bounds (psgd_pro.py:19, psgd_pro_fast.py:29)
 TT = 32     # tile edge of the element-wise kernels
@@ -184,6 +185,7 @@ class _Plan:
         off = 0
         for p in self.params:
             p.xi = self.xi[off:off + p.numel].view(p.n1, p.n2)
+            p.xi_off = off  # also the parameter's place in the generated noise sequence
             off += cdiv(p.numel, 4) * 4
         dense = [f for f in self.factors if f.kind == "dense"]
         self.vbuf = torch.zeros(sum(2 * K_SUB * f.n for f in dense), device=device)
@@ -231,6 +233,7 @@ class _Plan:
                 it = _capi.PrepItem()
                 it.g, it.g_bf16 = src.data_ptr(), int(src.dtype == torch.bfloat16)
                 it.xi = p.xi.data_ptr() if phase == "u" else None
+                it.noise_base = p.xi_off
                 it.n1, it.n2, it.eps = p.n1, p.n2, grad_eps[k]
                 it.p1 = p.f1.p.data_ptr() if p.f1.kind == "diag" else None
                 it.p2 = p.f2.p.data_ptr() if p.f2.kind == "diag" else None
@@ -623,6 +626,7 @@ class KronWhiten:
         self._graphs = {}
         self._hyper_host = None
         self._steps = 0
+        self._noise_key = None  # key word of the in-kernel noise generator, drawn from torch's RNG at the first step
         self.trace = None  # optional callable(name) run after every launch (profiling; disables graphs)
         _capi.lib()  # fail loudly now if the kernels are missing
         if preconditioner_init_scale is not None:
@@ -680,16 +684,23 @@ class KronWhiten:
         self._graphs = {}
 
     # ---- the step ------------------------------------------------------------------------------------------
-    def _set_hyper(self, beta_m=0.0):
+    def _set_hyper(self, beta_m=0.0, noise=None):
+        """Device hyper-parameter vector. noise: None (the damping noise is read from the draws buffer) or the
+        (key0, key1) of the in-kernel generator."""
         h = [0.0] * HY_COUNT
         h[HY_LR_PRECOND], h[HY_BETA_L], h[HY_DAMPING] = self.lr_preconditioner, self.betaL, self.damping
         h[HY_LR_PARAMS] = self.lr_params
         h[HY_MAX_AVG], h[HY_MAX_ELEM] = self.grad_clip_max_amps
         h[HY_MOM_BETA] = beta_m
-        h = tuple(float(x) for x in h)
-        if h != self._hyper_host:
-            self._plan.hyper.copy_(torch.tensor(h, dtype=torch.float32))
-            self._hyper_host = h
+        bits = [struct.unpack("<i", struct.pack("<f", float(x)))[0] for x in h]
+        if noise is not None:
+            bits[HY_NOISE] = struct.unpack("<i", struct.pack("<f", 1.0))[0]
+            bits[HY_NOISE_KEY0], bits[HY_NOISE_KEY1] = (struct.unpack("<i", struct.pack("<I", k & 0xFFFFFFFF))[0]
+                                                        for k in noise)
+        bits = tuple(bits)
+        if bits != self._hyper_host:
+            self._plan.hyper.view(torch.int32).copy_(torch.tensor(bits, dtype=torch.int32))
+            self._hyper_host = bits
 
     def _balance(self, ks):
         """psgd_pro.py:96-105 for the parameters ks whose coin fired (probability 0.01 each per step): one
@@ -756,7 +767,9 @@ class KronWhiten:
             self._graphs = {}
         elif (tuple(t.data_ptr() for t in src_u), tuple(t.data_ptr() for t in src_a)) != plan.grad_ptrs:
             plan.update_grad_ptrs(src_u, src_a)
-        self._set_hyper(beta)
+        if draws is None and self._noise_key is None:
+            self._noise_key = int(torch.randint(0, 2 ** 31, (1,)).item())
+        self._set_hyper(beta, noise=(self._noise_key, self._steps) if draws is None else None)
         if draws is None:
             update = bool(torch.rand([]) < self.preconditioner_update_probability)
             coins = (torch.rand(len(plan.params)) < 0.01).tolist() if update else []
@@ -774,8 +787,7 @@ class KronWhiten:
             trace("start")
 
         def upd():
-            if draws is None:
-                plan.xi.normal_()
+            if draws is None:  # the damping noise comes from the prep kernel's generator
                 plan.vbuf.normal_()
                 if trace is not None:
                     trace("rng")
