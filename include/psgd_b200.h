@@ -194,11 +194,23 @@ int psgd_factor_update(const PsgdFactorItem* items, int nitems, const float* hyp
  * (2 TI) * tiles32 + 2 TJ. Every other slot stays as the caller left it (zero: consumers sum or max over all). */
 #define PSGD_SKEW_TILE 64
 typedef struct PsgdSkewItem {
-  const float* q; int n;
+  float* q; int n;
   void* r_hi; void* r_lo; long long ldr;
   float* part_row; float* part_max; float* part_dot;
+  /* Rank-one factors (1-D parameters, psgd_pro.py:132-135 with term1 = Pg Pg^T): when u_hi != NULL the q update
+   * runs here first, q <- (*alpha) (u v^T) + (*beta) q with u = u_hi (+ u_lo) and v = v_hi (+ v_lo) the n-vectors
+   * stored one per row (leading dimensions ldu, ldv; the K = 1 operands of that product), summed hi * hi, + hi * lo,
+   * + lo * hi; the updated q is written back (fp32) and as q^T (bf16 hi/lo, qt_hi/qt_lo, leading dimension ldqt),
+   * and Rn is taken from the updated q. */
+  const void* u_hi; const void* u_lo; long long ldu;
+  const void* v_hi; const void* v_lo; long long ldv;
+  const float* alpha; const float* beta;
+  void* qt_hi; void* qt_lo; long long ldqt;
 } PsgdSkewItem;
 int psgd_skew(const PsgdSkewItem* items, const uint32_t* work, int nwork, int* dev_err, cudaStream_t stream);
+/* The same for work entries whose items carry the rank-one q update (u_hi != NULL); psgd_skew ignores those
+ * fields. No counterpart entry point in the reference: there the update is a separate product (psgd_pro.py:135). */
+int psgd_skew_rank1(const PsgdSkewItem* items, const uint32_t* work, int nwork, int* dev_err, cudaStream_t stream);
 
 /* M = a (Rn / s) + a^2 / 2 ((S / s) / s) (bf16 hi/lo in, bf16 hi/lo out in place of Rn), with a = *alpha and
  * 1/s = *beta from PSGD_FACTOR_SKEW: the Procrustes multiplier of psgd_pro_fast.py:153. Work entries: (item,

@@ -59,7 +59,9 @@ class FactorItem(ctypes.Structure):
 
 class SkewItem(ctypes.Structure):
     _fields_ = [("q", c_vp), ("n", c_int), ("r_hi", c_vp), ("r_lo", c_vp), ("ldr", c_ll), ("part_row", c_vp),
-                ("part_max", c_vp), ("part_dot", c_vp)]
+                ("part_max", c_vp), ("part_dot", c_vp), ("u_hi", c_vp), ("u_lo", c_vp), ("ldu", c_ll),
+                ("v_hi", c_vp), ("v_lo", c_vp), ("ldv", c_ll), ("alpha", c_vp), ("beta", c_vp),
+                ("qt_hi", c_vp), ("qt_lo", c_vp), ("ldqt", c_ll)]
 
 
 class RotItem(ctypes.Structure):
@@ -104,6 +106,7 @@ SIGNATURES = [
     ("psgd_nlb_prep", c_int, [c_vp, c_int, c_vp, c_vp]),
     ("psgd_factor_update", c_int, [c_vp, c_int, c_vp, c_vp, c_vp]),
     ("psgd_skew", c_int, [c_vp, c_vp, c_int, c_vp, c_vp]),
+    ("psgd_skew_rank1", c_int, [c_vp, c_vp, c_int, c_vp, c_vp]),
     ("psgd_rot", c_int, [c_vp, c_vp, c_int, c_vp, c_vp]),
     ("psgd_apply", c_int, [c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_vp]),
     ("psgd_balance", c_int, [c_vp, c_vp, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_vp]),

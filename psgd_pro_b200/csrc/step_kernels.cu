@@ -406,10 +406,33 @@ PSGD_DEVI float4 load4q(const float* __restrict__ q, int n, int row, int col0, b
   return v;
 }
 
-__global__ void __launch_bounds__(256) skew_kernel(const PsgdSkewItem* __restrict__ items,
-                                                  const uint32_t* __restrict__ work, int nwork) {
+// Q[row][col0 .. col0 + 3] = v (the in-range elements).
+PSGD_DEVI void store4q(float* __restrict__ q, int n, int row, int col0, bool vec, float4 v) {
+  if (row >= n) return;
+  float* dst = q + (long long)row * n + col0;
+  if (vec && col0 + 3 < n) {
+    *reinterpret_cast<float4*>(dst) = v;
+    return;
+  }
+  if (col0 < n) dst[0] = v.x;
+  if (col0 + 1 < n) dst[1] = v.y;
+  if (col0 + 2 < n) dst[2] = v.z;
+  if (col0 + 3 < n) dst[3] = v.w;
+}
+
+PSGD_DEVI float ldbf(const void* p, long long idx) {
+  return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[idx]);
+}
+
+// R1: the items carry the rank-one q update (u_hi != NULL); without it that code is compiled out, so the plain
+// kernel keeps its register count and occupancy.
+template <bool R1>
+__global__ void __launch_bounds__(256, R1 ? 3 : 4) skew_kernel(const PsgdSkewItem* __restrict__ items,
+                                                              const uint32_t* __restrict__ work, int nwork) {
   __shared__ float sA[SK][SK + 1], sB[SK][SK + 1];
   __shared__ float red[8][2];
+  // R1: u at the rows of A (i0 ..) and of B (j0 ..), v at the columns of A (j0 ..) and of B (i0 ..); hi and lo
+  __shared__ float suv[R1 ? 4 : 1][2][SK];
   const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
   const int rr = t >> 4, c4 = (t & 15) * 4;  // this thread: rows rr + 16 m, columns c4 .. c4 + 3 of a tile
   for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
@@ -423,6 +446,53 @@ __global__ void __launch_bounds__(256) skew_kernel(const PsgdSkewItem* __restric
     for (int m = 0; m < 4; ++m) {
       a[m] = load4q(it.q, n, i0 + rr + 16 * m, j0 + c4, vec);
       b[m] = diag ? a[m] : load4q(it.q, n, j0 + rr + 16 * m, i0 + c4, vec);
+    }
+    const bool r1 = R1 && it.u_hi != nullptr;
+    if (r1) {  // the rank-one q update of this pair of tiles, written back before Rn is formed from it
+      {  // the four 64-element segments of u and v this pair uses, one element per thread
+        const int seg = t >> 6, e = t & 63;
+        const int base = (seg == 0 || seg == 3) ? i0 : j0;
+        const int idx = min(base + e, n - 1);
+        const void* h = seg < 2 ? it.u_hi : it.v_hi;
+        const void* l = seg < 2 ? it.u_lo : it.v_lo;
+        const long long ld = seg < 2 ? it.ldu : it.ldv;
+        suv[seg][0][e] = ldbf(h, (long long)idx * ld);
+        suv[seg][1][e] = l ? ldbf(l, (long long)idx * ld) : 0.f;
+      }
+      __syncthreads();
+      const float al = *it.alpha, be = *it.beta;
+      float vha[4], vla[4], vhb[4], vlb[4];  // v at A's columns j0 + c4 + k and at B's columns i0 + c4 + k
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        vha[k] = suv[2][0][c4 + k];
+        vla[k] = suv[2][1][c4 + k];
+        vhb[k] = suv[3][0][c4 + k];
+        vlb[k] = suv[3][1][c4 + k];
+      }
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const int ia = i0 + rr + 16 * m, ib = j0 + rr + 16 * m;
+        const float uha = suv[0][0][rr + 16 * m], ula = suv[0][1][rr + 16 * m];
+        const float uhb = suv[1][0][rr + 16 * m], ulb = suv[1][1][rr + 16 * m];
+        float xa[4] = {a[m].x, a[m].y, a[m].z, a[m].w}, xb[4] = {b[m].x, b[m].y, b[m].z, b[m].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          // the K = 1 product as the tensor cores form it (hi * hi, then + hi * lo, then + lo * hi), then the
+          // q-update epilogue: alpha * acc + beta * q
+          float acc = uha * vha[k];
+          acc = fmaf(uha, vla[k], acc);
+          acc = fmaf(ula, vha[k], acc);
+          xa[k] = (ia < n && j0 + c4 + k < n) ? fmaf(be, xa[k], acc * al) : 0.f;
+          float bcc = uhb * vhb[k];
+          bcc = fmaf(uhb, vlb[k], bcc);
+          bcc = fmaf(ulb, vhb[k], bcc);
+          xb[k] = (ib < n && i0 + c4 + k < n) ? fmaf(be, xb[k], bcc * al) : 0.f;
+        }
+        a[m] = make_float4(xa[0], xa[1], xa[2], xa[3]);
+        b[m] = diag ? a[m] : make_float4(xb[0], xb[1], xb[2], xb[3]);
+        store4q(it.q, n, ia, j0 + c4, vec, a[m]);
+        if (!diag) store4q(it.q, n, ib, i0 + c4, vec, b[m]);
+      }
     }
     {
 #pragma unroll
@@ -464,6 +534,10 @@ __global__ void __launch_bounds__(256) skew_kernel(const PsgdSkewItem* __restric
           dsum += v[k] * x;
         }
         if (gi < n && nv > 0) st4_split(it.r_hi, it.r_lo, (long long)gi * it.ldr + gj0, v, vs, nv);
+        if (r1 && gi < n && nv > 0) {  // q^T of the updated q: its row gi is the transposed operand read above
+          const float yv[4] = {Y[c4][r], Y[c4 + 1][r], Y[c4 + 2][r], Y[c4 + 3][r]};
+          st4_split(it.qt_hi, it.qt_lo, (long long)gi * it.ldqt + gj0, yv, nv == 4 && (it.ldqt % 4) == 0, nv);
+        }
         rs += __shfl_xor_sync(0xffffffffu, rs, 1);
         rs += __shfl_xor_sync(0xffffffffu, rs, 2);
         rs += __shfl_xor_sync(0xffffffffu, rs, 4);
@@ -762,7 +836,15 @@ extern "C" int psgd_skew(const PsgdSkewItem* items, const uint32_t* work, int nw
                          cudaStream_t stream) {
   if (!items || !work || nwork < 0) return PSGD_EINVAL;
   if (nwork == 0) return PSGD_OK;
-  skew_kernel<<<grid_for(skew_kernel, 256, nwork), 256, 0, stream>>>(items, work, nwork);
+  skew_kernel<false><<<grid_for(skew_kernel<false>, 256, nwork), 256, 0, stream>>>(items, work, nwork);
+  return launched();
+}
+
+extern "C" int psgd_skew_rank1(const PsgdSkewItem* items, const uint32_t* work, int nwork, int* dev_err,
+                               cudaStream_t stream) {
+  if (!items || !work || nwork < 0) return PSGD_EINVAL;
+  if (nwork == 0) return PSGD_OK;
+  skew_kernel<true><<<grid_for(skew_kernel<true>, 256, nwork), 256, 0, stream>>>(items, work, nwork);
   return launched();
 }
 

@@ -325,29 +325,35 @@ class _Plan:
             fi.append(it)
         self.fac_dev, self.fac_n = _upload(_capi.FactorItem, fi, dev), len(fi)
         # U10: q <- q - lr/L (term1 q - term2 q)
-        u10, u10r = [], []
+        # (rank-one factors: the same update, q <- alpha Pg w^T + beta q, runs inside the skew kernel below)
+        u10 = []
         for f in dense:
-            kw = dict(alpha_ptr=self.s(f, S_AQ), beta_ptr=self.s(f, S_BQ), alpha=1.0, beta=1.0, aux=f.q,
-                      out_f32=f.q, out_hi_t=f.qtb[0], out_lo_t=f.qtb[1])
-            if f.rank1:
-                p = next(p for p in P if p.f2 is f)
-                u10r.append(self.spec(p.pgT, p.w, f.n, f.n, 1, **kw))
-            else:
-                u10.append(self.spec(f.T, f.qta, f.n, f.n, f.n, **kw))
-        self.g_u10, self.g_u10r = self.group(u10), self.group(u10r)
+            if not f.rank1:
+                u10.append(self.spec(f.T, f.qta, f.n, f.n, f.n, alpha_ptr=self.s(f, S_AQ), beta_ptr=self.s(f, S_BQ),
+                                     alpha=1.0, beta=1.0, aux=f.q, out_f32=f.q, out_hi_t=f.qtb[0],
+                                     out_lo_t=f.qtb[1]))
+        self.g_u10 = self.group(u10)
         # U11: Rn = Q - Q^T
-        sk, skw = [], []
+        sk, skw, skw1 = [], [], []
         for f in dense:
             it = _capi.SkewItem()
             it.q, it.n, it.r_hi, it.r_lo, it.ldr = f.q.data_ptr(), f.n, K.ptr(f.R[0]), K.ptr(f.R[1]), f.R[0].stride(0)
             it.part_row, it.part_max, it.part_dot = f.r_rows.data_ptr(), f.r_max.data_ptr(), f.r_dot.data_ptr()
+            if f.rank1:  # U10 for this factor: q <- alpha Pg w^T + beta q, q^T to qtb
+                p = next(p for p in P if p.f2 is f)
+                it.u_hi, it.u_lo, it.ldu = K.ptr(p.pgT[0]), K.ptr(p.pgT[1]), p.pgT[0].stride(0)
+                it.v_hi, it.v_lo, it.ldv = K.ptr(p.w[0]), K.ptr(p.w[1]), p.w[0].stride(0)
+                it.alpha, it.beta = self.s(f, S_AQ).data_ptr(), self.s(f, S_BQ).data_ptr()
+                it.qt_hi, it.qt_lo, it.ldqt = K.ptr(f.qtb[0]), K.ptr(f.qtb[1]), f.qtb[0].stride(0)
             sk.append(it)
             # pairs by diagonal (tj - ti, then ti): blocks running together read tiles at many row and column
             # offsets, not one column band of Q (whose rows sit a power-of-two stride apart)
             t64 = cdiv(f.n, _capi.SKEW_TILE)
-            skw += [(len(sk) - 1, (ti << 16) | (ti + d)) for d in range(t64) for ti in range(t64 - d)]
+            (skw1 if f.rank1 else skw).extend((len(sk) - 1, (ti << 16) | (ti + d)) for d in range(t64)
+                                              for ti in range(t64 - d))
         self.skew_dev = _upload(_capi.SkewItem, sk, dev)
         self.skew_work, self.skew_n = _work(skw, dev)
+        self.skew1_work, self.skew1_n = _work(skw1, dev)
         # U12..U16: norm lower bound of Rn (skew)
         self.nlb_skh_dev, self.nlb_skh_n = self._nlb_prep(dense, skew=True)
         self.g_skh = self._nlb_chain(dense, skew=True)
@@ -522,10 +528,10 @@ class _Plan:
         tr("factor")
         self._launch(self.g_u10)
         tr("qupdate")
-        self._launch(self.g_u10r)
-        tr("qupdate_r1")
         check(L.psgd_skew(self.skew_dev.data_ptr(), self.skew_work.data_ptr(), self.skew_n, err, st), "skew")
         tr("skew")
+        check(L.psgd_skew_rank1(self.skew_dev.data_ptr(), self.skew1_work.data_ptr(), self.skew1_n, err, st), "skew r1")
+        tr("skew_r1")
         check(L.psgd_nlb_prep(self.nlb_skh_dev.data_ptr(), self.nlb_skh_n, err, st), "nlb_prep skh")
         tr("nlb_prep_skh")
         for k, g in enumerate(self.g_skh):
@@ -559,7 +565,7 @@ class _Plan:
         """(name, GemmGroup) of every tensor-core phase, in the names run_update / run_apply trace."""
         out = [("u1", self.g_u1), ("u2", self.g_u2), ("term1", self.g_u3), ("term1_r1", self.g_u3r)]
         out += [(f"nlb_spd{k}", g) for k, g in enumerate(self.g_spd)]
-        out += [("qupdate", self.g_u10), ("qupdate_r1", self.g_u10r)]
+        out += [("qupdate", self.g_u10)]
         out += [(f"nlb_skh{k}", g) for k, g in enumerate(self.g_skh)]
         out += [("S", self.g_u17), ("procrustes", self.g_u20), ("gram", self.g_u22), ("a1", self.g_a1),
                 ("a2", self.g_a2)]
@@ -570,10 +576,10 @@ class _Plan:
         n = 3  # prep, clip scale, apply
         groups = [self.g_a1, self.g_a2]
         if update:
-            n += 1 + 2 * int(self.nlb_spd_n > 0) + 2 + 2 * int(self.skew_n > 0)  # prep, nlb preps, factor x2, skew, rot
+            n += 1 + 2 * int(self.nlb_spd_n > 0) + 2 + int(self.skew_n > 0) + int(self.skew1_n > 0)
+            n += int(self.skew_n + self.skew1_n > 0)  # prep, nlb preps, factor x2, skew (two kinds), rot
             n -= int(self.skf_n == 0)
-            groups += [self.g_u1, self.g_u2, self.g_u3, self.g_u3r, self.g_u10, self.g_u10r, self.g_u17, self.g_u20,
-                       self.g_u22]
+            groups += [self.g_u1, self.g_u2, self.g_u3, self.g_u3r, self.g_u10, self.g_u17, self.g_u20, self.g_u22]
             groups += self.g_spd + self.g_skh
         return n + sum(g is not None for g in groups)
 
