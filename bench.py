@@ -287,10 +287,18 @@ def main():
         flops = groups[dominant].flops
         achieved = flops / (tm * 1e-3) / 1e12
         peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+        kind = groups[dominant].kind
+        kernel = (f"gemm_pair_kernel<256,6,{kind & 7}>" if kind & 8 else
+                  (f"gemm_group_kernel<1,256,4,{kind}>" if inner._split == 1 else f"gemm_group_kernel<3,128,3,{kind}>"))
+        # DRAM traffic of the q-update / Procrustes pair kernel, from one ncu capture (dram__bytes_read.sum +
+        # dram__bytes_write.sum) of the Procrustes launch of the one-layer Llama case (the same factor sizes),
+        # scaled to this launch by FLOPs: 3.357 GB for 1.2609 TFLOP
+        traffic = None
+        if dominant in ("procrustes", "qupdate") and kind == 9:
+            traffic = flops * (3.357e9 / 1.2609e12)
         roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                    "frac": achieved / peak, "traffic": None, "kernel": "gemm_group_kernel<1,256,4>" if
-                    inner._split == 1 else "gemm_group_kernel<3,128,3>", "phase": dominant,
-                    "flops_per_launch": flops, "ms_per_launch": tm,
+                    "frac": achieved / peak, "traffic": traffic, "traffic_unit": "bytes per launch",
+                    "kernel": kernel, "phase": dominant, "flops_per_launch": flops, "ms_per_launch": tm,
                     "peak_source": f"{peak_src} sustained bf16 (MEASURED_PEAKS.json)" if peak_src == "measured"
                     else "fallback"}
 
