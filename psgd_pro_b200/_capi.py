@@ -6,7 +6,7 @@ import ctypes
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "_lib", "libpsgd_b200.so")
+LIB_PATH = os.environ.get("PSGD_B200_LIB") or os.path.join(_HERE, "_lib", "libpsgd_b200.so")  # env: another build
 
 c_vp, c_ll, c_int, c_float = ctypes.c_void_p, ctypes.c_longlong, ctypes.c_int, ctypes.c_float
 c_fp = ctypes.POINTER(ctypes.c_float)

@@ -55,10 +55,13 @@ PSGD_DEVI float4 normal4(unsigned long long blk, uint32_t k0, uint32_t k1) {
   constexpr float inv32 = 2.3283064365386963e-10f;  // 2^-32: uniforms (w + 1/2) / 2^32 in (0, 1)
   const float u0 = ((float)w.x + 0.5f) * inv32, u1 = ((float)w.y + 0.5f) * inv32;
   const float u2 = ((float)w.z + 0.5f) * inv32, u3 = ((float)w.w + 0.5f) * inv32;
-  const float r0 = sqrtf(-2.f * logf(u0)), r1 = sqrtf(-2.f * logf(u2));
+  // hardware approximations of log, sin and cos (errors near 1e-6, far below what damping noise needs); the
+  // angle 2 pi u - pi lies in [-pi, pi), where __sincosf is most accurate
+  const float r0 = sqrtf(-2.f * __logf(u0)), r1 = sqrtf(-2.f * __logf(u2));
+  constexpr float TWO_PI = 6.2831853071795865f, PI = 3.1415926535897932f;
   float s0, c0, s1, c1;
-  sincospif(2.f * u1, &s0, &c0);
-  sincospif(2.f * u3, &s1, &c1);
+  __sincosf(TWO_PI * u1 - PI, &s0, &c0);
+  __sincosf(TWO_PI * u3 - PI, &s1, &c1);
   return make_float4(r0 * c0, r0 * s0, r1 * c1, r1 * s1);
 }
 

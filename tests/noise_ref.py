@@ -1,6 +1,6 @@
 """Test-side restatement of the in-kernel damping-noise generator (psgd_prep with hyper[PSGD_HY_NOISE] set):
 Philox4x32-10 (Salmon, Moraes, Dror and Shaw, SC'11) on counter (s / 4, 0, 0, 0) with a 2-word key, the four words
-turned into four standard normal numbers by two Box-Muller transforms. numpy, float64 transforms."""
+turned into four standard normal numbers by two Box-Muller transforms (angles 2 pi u - pi). numpy, float64 transforms."""
 import numpy as np
 
 M0, M1, W0, W1 = 0xD2511F53, 0xCD9E8D57, 0x9E3779B9, 0xBB67AE85
@@ -30,6 +30,6 @@ def normals(positions, k0, k1):
     w = philox4x32_10(c, (k0, k1)).astype(np.float64)
     u = (w + 0.5) * 2.0 ** -32
     r0, r1 = np.sqrt(-2 * np.log(u[..., 0])), np.sqrt(-2 * np.log(u[..., 2]))
-    z = np.stack([r0 * np.cos(2 * np.pi * u[..., 1]), r0 * np.sin(2 * np.pi * u[..., 1]),
-                  r1 * np.cos(2 * np.pi * u[..., 3]), r1 * np.sin(2 * np.pi * u[..., 3])], axis=-1)
+    t1, t3 = 2 * np.pi * u[..., 1] - np.pi, 2 * np.pi * u[..., 3] - np.pi
+    z = np.stack([r0 * np.cos(t1), r0 * np.sin(t1), r1 * np.cos(t3), r1 * np.sin(t3)], axis=-1)
     return np.take_along_axis(z, (pos & np.uint64(3)).astype(np.int64)[..., None], axis=-1)[..., 0]
