@@ -224,7 +224,9 @@ typedef struct PsgdRotItem {
   const void* s_hi; const void* s_lo; long long lds;
   const float* alpha; const float* beta;
 } PsgdRotItem;
-int psgd_rot(const PsgdRotItem* items, const uint32_t* work, int nwork, int* dev_err, cudaStream_t stream);
+/* has_lo: the items' r_lo / s_lo are set (fp32 mode; with 0 they are ignored). */
+int psgd_rot(const PsgdRotItem* items, const uint32_t* work, int nwork, int has_lo, int* dev_err,
+             cudaStream_t stream);
 
 /* Clip and apply (psgd_pro.py:371-381, branch-free as psgd_pro_fast.py:426-438): per parameter
  * avg = sqrt(sum(part) / numel), g = clamp(pg * min(1, max_avg / avg), +-max_elem), param -= lr_params * g.

@@ -107,7 +107,7 @@ SIGNATURES = [
     ("psgd_factor_update", c_int, [c_vp, c_int, c_vp, c_vp, c_vp]),
     ("psgd_skew", c_int, [c_vp, c_vp, c_int, c_vp, c_vp]),
     ("psgd_skew_rank1", c_int, [c_vp, c_vp, c_int, c_vp, c_vp]),
-    ("psgd_rot", c_int, [c_vp, c_vp, c_int, c_vp, c_vp]),
+    ("psgd_rot", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp]),
     ("psgd_apply", c_int, [c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_vp]),
     ("psgd_balance", c_int, [c_vp, c_vp, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_vp]),
     ("psgd_apply_noalloc", c_int, [c_vp, c_int, c_vp, c_ll, c_float, c_float, c_float, c_vp]),

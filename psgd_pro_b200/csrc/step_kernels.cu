@@ -581,6 +581,9 @@ PSGD_DEVI void unpack8(const uint4& u, float* f) {
   for (int i = 0; i < 8; ++i) f[i] = __bfloat162float(h[i]);
 }
 
+// LO: the operands carry lo halves (fp32 mode); without them that code is compiled out (fewer registers, more
+// blocks per SM).
+template <bool LO>
 __global__ void __launch_bounds__(256) rot_kernel(const PsgdRotItem* __restrict__ items,
                                                  const uint32_t* __restrict__ work, int nwork) {
   for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
@@ -590,9 +593,9 @@ __global__ void __launch_bounds__(256) rot_kernel(const PsgdRotItem* __restrict_
     const int nvec = (int)(it.ldr / 8);
     const int total = min(ROT_ROWS, it.n - r0) * nvec;
     __nv_bfloat16* rbase_h = reinterpret_cast<__nv_bfloat16*>(it.r_hi);
-    __nv_bfloat16* rbase_l = reinterpret_cast<__nv_bfloat16*>(it.r_lo);
+    __nv_bfloat16* rbase_l = LO ? reinterpret_cast<__nv_bfloat16*>(it.r_lo) : nullptr;
     const __nv_bfloat16* sbase_h = reinterpret_cast<const __nv_bfloat16*>(it.s_hi);
-    const __nv_bfloat16* sbase_l = reinterpret_cast<const __nv_bfloat16*>(it.s_lo);
+    const __nv_bfloat16* sbase_l = LO ? reinterpret_cast<const __nv_bfloat16*>(it.s_lo) : nullptr;
     for (int k0 = threadIdx.x; k0 < total; k0 += ROT_VEC * blockDim.x) {
       uint4 rh[ROT_VEC], sh[ROT_VEC], rl[ROT_VEC], sl[ROT_VEC];
       long long ro[ROT_VEC], so[ROT_VEC];
@@ -605,8 +608,8 @@ __global__ void __launch_bounds__(256) rot_kernel(const PsgdRotItem* __restrict_
         if (k < total) {
           rh[u] = *reinterpret_cast<const uint4*>(rbase_h + ro[u]);
           sh[u] = *reinterpret_cast<const uint4*>(sbase_h + so[u]);
-          if (rbase_l) rl[u] = *reinterpret_cast<const uint4*>(rbase_l + ro[u]);
-          if (sbase_l) sl[u] = *reinterpret_cast<const uint4*>(sbase_l + so[u]);
+          if (LO && rbase_l) rl[u] = *reinterpret_cast<const uint4*>(rbase_l + ro[u]);
+          if (LO && sbase_l) sl[u] = *reinterpret_cast<const uint4*>(sbase_l + so[u]);
         }
       }
 #pragma unroll
@@ -615,13 +618,13 @@ __global__ void __launch_bounds__(256) rot_kernel(const PsgdRotItem* __restrict_
         float rv[8], sv[8];
         unpack8(rh[u], rv);
         unpack8(sh[u], sv);
-        if (rbase_l) {
+        if (LO && rbase_l) {
           float l[8];
           unpack8(rl[u], l);
 #pragma unroll
           for (int i = 0; i < 8; ++i) rv[i] += l[i];
         }
-        if (sbase_l) {
+        if (LO && sbase_l) {
           float l[8];
           unpack8(sl[u], l);
 #pragma unroll
@@ -631,7 +634,7 @@ __global__ void __launch_bounds__(256) rot_kernel(const PsgdRotItem* __restrict_
 #pragma unroll
         for (int i = 0; i < 8; ++i) split_bf16(a * (rv[i] * inv_s) + half_a2 * ((sv[i] * inv_s) * inv_s), h[i], l[i]);
         *reinterpret_cast<uint4*>(rbase_h + ro[u]) = *reinterpret_cast<const uint4*>(h);
-        if (rbase_l) *reinterpret_cast<uint4*>(rbase_l + ro[u]) = *reinterpret_cast<const uint4*>(l);
+        if (LO && rbase_l) *reinterpret_cast<uint4*>(rbase_l + ro[u]) = *reinterpret_cast<const uint4*>(l);
       }
     }
   }
@@ -851,11 +854,12 @@ extern "C" int psgd_skew_rank1(const PsgdSkewItem* items, const uint32_t* work, 
   return launched();
 }
 
-extern "C" int psgd_rot(const PsgdRotItem* items, const uint32_t* work, int nwork, int* dev_err,
+extern "C" int psgd_rot(const PsgdRotItem* items, const uint32_t* work, int nwork, int has_lo, int* dev_err,
                         cudaStream_t stream) {
   if (!items || !work || nwork < 0) return PSGD_EINVAL;
   if (nwork == 0) return PSGD_OK;
-  rot_kernel<<<grid_for(rot_kernel, 256, nwork), 256, 0, stream>>>(items, work, nwork);
+  if (has_lo) rot_kernel<true><<<grid_for(rot_kernel<true>, 256, nwork), 256, 0, stream>>>(items, work, nwork);
+  else rot_kernel<false><<<grid_for(rot_kernel<false>, 256, nwork), 256, 0, stream>>>(items, work, nwork);
   return launched();
 }
 

@@ -541,7 +541,8 @@ class _Plan:
         tr("S")
         check(L.psgd_factor_update(self.skf_dev.data_ptr(), self.skf_n, hy, err, st), "procrustes scalars")
         tr("procrustes_scalars")
-        check(L.psgd_rot(self.rot_dev.data_ptr(), self.rot_work.data_ptr(), self.rot_n, err, st), "rot")
+        check(L.psgd_rot(self.rot_dev.data_ptr(), self.rot_work.data_ptr(), self.rot_n, int(self.split == 3), err, st),
+              "rot")
         tr("rot")
         self._launch(self.g_u20)
         tr("procrustes")
