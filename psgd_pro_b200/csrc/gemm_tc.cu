@@ -39,13 +39,17 @@ struct GemmCfg {
   static constexpr int NOPS = SPLIT == 1 ? 1 : 2;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BNMAX * BK * 2;
-  static constexpr int STAGE_BYTES = NOPS * (A_BYTES + B_BYTES);
+  // Narrow tiles (memory-bound streams of the A panel) take KSUB consecutive 64-deep K blocks per stage, so every
+  // A row is read in KSUB * 128-byte runs.
+  static constexpr int KSUB = (SPLIT == 1 && BNMAX <= 64) ? 4 : 1;
+  static constexpr int SUB_BYTES = NOPS * (A_BYTES + B_BYTES);
+  static constexpr int STAGE_BYTES = KSUB * SUB_BYTES;
   static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
   static constexpr int TMEM_COLS = 2 * BNMAX;
   static constexpr int CTRL_BYTES = 256;  // barriers, TMEM slot, abort flag
   static constexpr int RED_FLOATS = 4 * BNMAX + BNMAX + 32 + 4 * 32 * 36;  // + the staging blocks
   static constexpr int SMEM_BYTES = 1024 + TILE_BYTES + CTRL_BYTES + RED_FLOATS * 4;
-  static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
+  static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
 };
 
 // ---- epilogue ------------------------------------------------------------------------------------------------
@@ -814,21 +818,26 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
         int p, tm, tn;
         get_tile(descs, tiles, t, p, tm, tn);
         const GemmDesc& d = descs[p];
-        const int nk = (d.s.K + BK - 1) / BK;
-        const uint32_t bytes = C::NOPS * (C::A_BYTES + d.s.bn * BK * 2);
+        const int nk = (d.s.K + BK * C::KSUB - 1) / (BK * C::KSUB);
+        const uint32_t sub_bytes = C::NOPS * (C::A_BYTES + d.s.bn * BK * 2);
         for (int kb = 0; kb < nk; ++kb, ++g) {
           const int s = g % STAGES;
           const uint32_t ph = (g / STAGES) & 1;
+          // 64-deep blocks of this stage that hold any of K (no copy is issued past the end)
+          const int nsub = min(C::KSUB, (d.s.K - kb * BK * C::KSUB + BK - 1) / BK);
           if (!mbar_wait(&empty[s], ph ^ 1, abort)) break;
-          mbar_arrive_expect_tx(&full[s], bytes);
+          mbar_arrive_expect_tx(&full[s], sub_bytes * (uint32_t)nsub);
           armed[s] += 1;
-          uint8_t* sa = smem + s * C::STAGE_BYTES;
-          uint8_t* sb = sa + C::NOPS * C::A_BYTES;
-          tma_load_2d(sa, &d.ta[0], &full[s], kb * BK, tm * BM);
-          tma_load_2d(sb, &d.tb[0], &full[s], kb * BK, tn * d.s.bn);
-          if (SPLIT != 1) {
-            tma_load_2d(sa + C::A_BYTES, &d.ta[1], &full[s], kb * BK, tm * BM);
-            tma_load_2d(sb + C::B_BYTES, &d.tb[1], &full[s], kb * BK, tn * d.s.bn);
+          for (int j = 0; j < nsub; ++j) {
+            uint8_t* sa = smem + s * C::STAGE_BYTES + j * C::SUB_BYTES;
+            uint8_t* sb = sa + C::NOPS * C::A_BYTES;
+            const int x = (kb * C::KSUB + j) * BK;
+            tma_load_2d(sa, &d.ta[0], &full[s], x, tm * BM);
+            tma_load_2d(sb, &d.tb[0], &full[s], x, tn * d.s.bn);
+            if (SPLIT != 1) {
+              tma_load_2d(sa + C::A_BYTES, &d.ta[1], &full[s], x, tm * BM);
+              tma_load_2d(sb + C::B_BYTES, &d.tb[1], &full[s], x, tn * d.s.bn);
+            }
           }
         }
       }
@@ -849,7 +858,7 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
         int p, tm, tn;
         get_tile(descs, tiles, t, p, tm, tn);
         const GemmDesc& d = descs[p];
-        const int nk = (d.s.K + BK - 1) / BK;
+        const int nk = (d.s.K + BK * C::KSUB - 1) / (BK * C::KSUB);
         const int bn = d.s.bn;
         const uint32_t acc = i & 1, aph = (i >> 1) & 1;
         if (!mbar_wait(&tempty[acc], aph ^ 1, abort)) break;
@@ -865,15 +874,18 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
             break;
           }
           tc_fence_after();
-          const uint32_t a_hi = smem_u32(smem + s * C::STAGE_BYTES);
-          const uint32_t b_hi = a_hi + C::NOPS * C::A_BYTES;
+          const int nsub = min(C::KSUB, (d.s.K - kb * BK * C::KSUB + BK - 1) / BK);
+          for (int j = 0; j < nsub; ++j) {
+            const uint32_t a_hi = smem_u32(smem + s * C::STAGE_BYTES + j * C::SUB_BYTES);
+            const uint32_t b_hi = a_hi + C::NOPS * C::A_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t ad = sdesc_k_sw128(a_hi + kk * 32), bd = sdesc_k_sw128(b_hi + kk * 32);
-            umma_bf16(dt, ad, bd, idesc, (kb | kk) != 0);
-            if (SPLIT != 1) {
-              umma_bf16(dt, ad, sdesc_k_sw128(b_hi + C::B_BYTES + kk * 32), idesc, 1);
-              umma_bf16(dt, sdesc_k_sw128(a_hi + C::A_BYTES + kk * 32), bd, idesc, 1);
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              const uint64_t ad = sdesc_k_sw128(a_hi + kk * 32), bd = sdesc_k_sw128(b_hi + kk * 32);
+              umma_bf16(dt, ad, bd, idesc, (kb | j | kk) != 0);
+              if (SPLIT != 1) {
+                umma_bf16(dt, ad, sdesc_k_sw128(b_hi + C::B_BYTES + kk * 32), idesc, 1);
+                umma_bf16(dt, sdesc_k_sw128(a_hi + C::A_BYTES + kk * 32), bd, idesc, 1);
+              }
             }
           }
           issued = true;
@@ -972,7 +984,7 @@ struct PairCfg {
   static constexpr int CTRL_BYTES = 512;
   static constexpr int RED_FLOATS = 4 * BNMAX + BNMAX + 32 + 4 * 32 * 36;
   static constexpr int SMEM_BYTES = 1024 + TILE_BYTES + CTRL_BYTES + RED_FLOATS * 4;
-  static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
+  static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
   static_assert((3 * STAGES + 5) * 8 + 8 <= CTRL_BYTES, "barriers must fit the control block");
 };
 constexpr int PBM = 2 * BM;  // rows of a pair tile
@@ -1339,7 +1351,8 @@ static int launch_single(const GemmDesc& desc, const uint32_t* tiles, int ntiles
 
 // ---- pair kernel launch: one cluster of two CTAs per segment of the tile list ----
 constexpr int PAIR_BN = 256, PAIR_STAGES = 6;
-constexpr int KIND_PAIR = 8;  // flag in the encoded kind: the group runs on the pair kernel
+constexpr int KIND_PAIR = 8;     // flag in the encoded kind: the group runs on the pair kernel
+constexpr int KIND_NARROW = 16;  // flag: every tile is at most 64 columns wide (one-CTA kernel, long K stages)
 
 // Clusters a pair launch uses on the current device: as many as can be resident at once (at most SMs / 2).
 static int pair_clusters() {
@@ -1497,7 +1510,11 @@ extern "C" int psgd_gemm_encode(const PsgdGemmSpec* specs, int nspecs, void* hos
   int best = EPI_GENERIC;
   for (int t = 1; t < 5; ++t)
     if (w[t] > w[best] || (best == EPI_GENERIC && w[t] > 0)) best = t;
-  *kind = best | (pair ? KIND_PAIR : 0);
+  // Narrow groups (the N = 32 norm-bound products, the rank-one products) are memory-bound streams of their A
+  // operand: they run on a configuration for tiles up to 64 wide whose stages hold four 64-deep K blocks.
+  bool narrow = !pair;
+  for (int i = 0; i < nspecs && narrow; ++i) narrow = specs[i].bn <= 64 && !specs[i].a_lo && !specs[i].b_lo;
+  *kind = best | (pair ? KIND_PAIR : 0) | (narrow ? KIND_NARROW : 0);
 
   // Tiles in their natural order (problems as given, row-major within each), each handed to the CTA with the
   // least estimated work so far: neighbouring tiles (which share operand panels in L2) run at about the same
@@ -1543,11 +1560,14 @@ extern "C" int psgd_gemm_encode(const PsgdGemmSpec* specs, int nspecs, void* hos
 
 extern "C" int psgd_gemm_launch(const void* dev_table, const uint32_t* dev_tiles, int ntiles, int split, int kind,
                                 int* dev_err, cudaStream_t stream) {
-  if (!dev_table || !dev_tiles || ntiles < 0 || !dev_err || kind < 0 || (kind & 7) > 4 || kind > (KIND_PAIR | 4))
+  if (!dev_table || !dev_tiles || ntiles < 0 || !dev_err || kind < 0 || (kind & 7) > 4 ||
+      (kind & ~(7 | KIND_PAIR | KIND_NARROW)) != 0 || ((kind & KIND_PAIR) && (kind & KIND_NARROW)))
     return PSGD_EINVAL;
   if (ntiles == 0) return PSGD_OK;
   const GemmDesc* d = reinterpret_cast<const GemmDesc*>(dev_table);
   if (kind & KIND_PAIR) return split == 1 ? launch_pair_kind(d, dev_tiles, kind & 7, dev_err, stream) : PSGD_EINVAL;
+  if (kind & KIND_NARROW)
+    return split == 1 ? launch_group_kind<1, 64, 2>(d, dev_tiles, ntiles, kind & 7, dev_err, stream) : PSGD_EINVAL;
   if (split == 1) return launch_group_kind<1, 256, 4>(d, dev_tiles, ntiles, kind, dev_err, stream);
   if (split == 3) return launch_group_kind<3, 128, 3>(d, dev_tiles, ntiles, kind, dev_err, stream);
   return PSGD_EINVAL;

@@ -265,3 +265,28 @@ def test_pair_kernel_aux_epilogue(cuda, monkeypatch):
     assert rel(q, ref) < 1e-5
     assert rel(q, q1) < 1e-6
     assert rel(qt[:, :n].float(), q.T) < 1e-2
+
+
+def test_narrow_group_long_stages(cuda):
+    """Groups whose tiles are all at most 64 wide run on the narrow configuration (four 64-deep K blocks per stage):
+    K that ends inside a stage, K = 1, and every narrow width."""
+    g = torch.Generator().manual_seed(43)
+    shapes = [(512, 32, 1000, 32), (300, 10, 65, 16), (1024, 64, 300, 64), (128, 32, 1, 32), (700, 48, 257, 64)]
+    specs, refs, outs, keep = [], [], [], []
+    for (M, N, Kd, bn) in shapes:
+        a, A = bf16_operand(M, Kd, cuda, g)
+        b, B = bf16_operand(N, Kd, cuda, g)
+        keep += [A, B]
+        out = torch.full((M, N), float("nan"), device=cuda)
+        specs.append(K.make_spec(A, B, M, N, Kd, bn=bn, out_f32=out))
+        outs.append(out)
+        refs.append(A[0][:, :Kd].double() @ B[0][:, :Kd].double().T)
+    grp = K.GemmGroup(specs, 1, cuda, keep=keep)
+    assert grp.kind & 16  # the narrow configuration
+    err = err_word(cuda)
+    grp.launch(err)
+    grp.launch(err)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    for o, r in zip(outs, refs):
+        assert rel(o, r) < 1e-5
