@@ -223,6 +223,7 @@ class _Plan:
         dev, split = self.device, self.split
         P = self.params
         self.grad_ptrs = (tuple(t.data_ptr() for t in src_update), tuple(t.data_ptr() for t in src_apply))
+        self._ptr_items = {}
         # U0 / A0: gradient staging
         self.prep_u, self.prep_a = [], []
         pu, pa = [], []
@@ -490,14 +491,24 @@ class _Plan:
         return groups
 
     def update_grad_ptrs(self, src_update, src_apply):
-        """Re-point the staging items at this step's gradient tensors (only when their addresses changed)."""
+        """Re-point the staging items at this step's gradient tensors (only when their addresses changed). The item
+        arrays of each address set are built on the device once; switching sets is a device-to-device copy into
+        the live arrays (stream-ordered, no host wait, captured graphs stay valid)."""
         ptrs = (tuple(t.data_ptr() for t in src_update), tuple(t.data_ptr() for t in src_apply))
         if ptrs == self.grad_ptrs:
             return
-        for items, dev, src in ((self.prep_u, self.prep_u_dev, src_update), (self.prep_a, self.prep_a_dev, src_apply)):
-            for it, t in zip(items, src):
-                it.g, it.g_bf16 = t.data_ptr(), int(t.dtype == torch.bfloat16)
-            dev.copy_(_upload(_capi.PrepItem, items, "cpu"))
+        cached = self._ptr_items.get(ptrs)
+        if cached is None:
+            cached = []
+            for items, src in ((self.prep_u, src_update), (self.prep_a, src_apply)):
+                for it, t in zip(items, src):
+                    it.g, it.g_bf16 = t.data_ptr(), int(t.dtype == torch.bfloat16)
+                cached.append(_upload(_capi.PrepItem, items, self.device))
+            if len(self._ptr_items) >= 8:  # a handful of gradient buffers in rotation at most
+                self._ptr_items.clear()
+            self._ptr_items[ptrs] = cached
+        self.prep_u_dev.copy_(cached[0], non_blocking=True)
+        self.prep_a_dev.copy_(cached[1], non_blocking=True)
         self.grad_ptrs = ptrs
 
     # ---- launches ------------------------------------------------------------------------------------------------
