@@ -13,6 +13,7 @@ namespace psgd {
 constexpr int TT = 32;        // tile edge of the tiled element-wise kernels
 constexpr int TROWS = 8;      // threads per tile column (256 threads, 4 rows each)
 constexpr int PREP_ROWS = PSGD_PREP_ROWS;  // rows per work entry of the row-vector staging path
+constexpr int PREP_SUB = 4;                // rows a thread stages at once (loads in flight)
 
 PSGD_DEVI float load_g(const void* g, int bf16, long long idx) {
   return bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(g)[idx])
@@ -93,34 +94,47 @@ __global__ void __launch_bounds__(256) prep_kernel(const PsgdPrepItem* __restric
                        (it.xi == nullptr || (reinterpret_cast<uintptr_t>(it.xi) & 15) == 0) &&
                        (it.noise_base & 3) == 0;
       if (vec) {
+        // one 4-column vector per thread across PREP_SUB rows at a time: PREP_SUB gradient loads in flight per
+        // thread, no index divisions
         const int nv = it.n2 / 4;
-        for (int k = threadIdx.x; k < rows * nv; k += blockDim.x) {
-          const long long row = r0 + k / nv, col = (long long)(k % nv) * 4;
-          const long long idx = row * it.n2 + col;
-          float x[4];
-          if (it.g_bf16) {
-            const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(it.g) + idx);
-            const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+        for (int kv = threadIdx.x; kv < nv; kv += blockDim.x) {
+          const long long col = (long long)kv * 4;
+          for (int rs = 0; rs < rows; rs += PREP_SUB) {
+            float x[PREP_SUB][4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) x[i] = __bfloat162float(h[i]);
-          } else {
-            const float4 v = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(it.g) + idx);
-            x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+            for (int r = 0; r < PREP_SUB; ++r) {
+              if (rs + r >= rows) break;
+              const long long idx = (r0 + rs + r) * it.n2 + col;
+              if (it.g_bf16) {
+                const uint2 gv = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(it.g) + idx);
+                const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&gv);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) x[r][i] = __bfloat162float(h[i]);
+              } else {
+                const float4 v = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(it.g) + idx);
+                x[r][0] = v.x; x[r][1] = v.y; x[r][2] = v.z; x[r][3] = v.w;
+              }
+            }
+#pragma unroll
+            for (int r = 0; r < PREP_SUB; ++r) {
+              if (rs + r >= rows) break;
+              const long long row = r0 + rs + r, idx = row * it.n2 + col;
+              if (it.xi) {
+                const float4 z = gen ? normal4((unsigned long long)(it.noise_base + idx) >> 2, k0, k1)
+                                     : *reinterpret_cast<const float4*>(it.xi + idx);
+                const float zz[4] = {z.x, z.y, z.z, z.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) x[r][i] += (damping + it.eps * fabsf(x[r][i])) * zz[i];
+              }
+              __align__(8) __nv_bfloat16 h[4], l[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) split_bf16(x[r][i], h[i], l[i]);
+              const long long o = row * it.ld_out + col;
+              *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(it.out_hi) + o) = *reinterpret_cast<const uint2*>(h);
+              if (it.out_lo)
+                *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(it.out_lo) + o) = *reinterpret_cast<const uint2*>(l);
+            }
           }
-          if (it.xi) {
-            const float4 z = gen ? normal4((unsigned long long)(it.noise_base + idx) >> 2, k0, k1)
-                                 : *reinterpret_cast<const float4*>(it.xi + idx);
-            const float zz[4] = {z.x, z.y, z.z, z.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) x[i] += (damping + it.eps * fabsf(x[i])) * zz[i];
-          }
-          __align__(8) __nv_bfloat16 h[4], l[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) split_bf16(x[i], h[i], l[i]);
-          const long long o = row * it.ld_out + col;
-          *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(it.out_hi) + o) = *reinterpret_cast<const uint2*>(h);
-          if (it.out_lo)
-            *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(it.out_lo) + o) = *reinterpret_cast<const uint2*>(l);
         }
       } else {
         for (int k = threadIdx.x; k < rows * it.n2; k += blockDim.x) {
