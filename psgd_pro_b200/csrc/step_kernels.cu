@@ -386,8 +386,8 @@ __global__ void __launch_bounds__(FAC_THREADS) factor_kernel(const PsgdFactorIte
 }
 
 // ---- Rn = Q - Q^T ------------------------------------------------------------------------------------------------
-// One block per pair of 64 x 64 tiles (TI <= TJ): A = Q[TI, TJ] and B = Q[TJ, TI] are read once (a warp load
-// covers two 256-byte tile rows; float4 when n % 4 == 0), all requested before the first barrier, and both Rn
+// Work entries are pairs of 64 x 64 tiles (TI <= TJ): A = Q[TI, TJ] and B = Q[TJ, TI] are read once into shared
+// memory by cp.async (16-byte chunks when n % 4 == 0, a warp request covering two 256-byte tile rows), and both Rn
 // tiles, Rn[TI, TJ] = A - B^T and Rn[TJ, TI] = B - A^T, are written (8-byte bf16 stores). The reductions go to the
 // 32-wide slot layout of PsgdSkewItem: row sums into slot 2 TJ (or 2 TI), the pair's max and trace share into entry
 // (2 TI) * tiles32 + 2 TJ; the slots no block writes stay zero.
@@ -441,42 +441,107 @@ PSGD_DEVI float ldbf(const void* p, long long idx) {
   return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[idx]);
 }
 
+// Shared-memory tile of the skew kernel: row r of a 64 x 64 fp32 tile starts at float r * 64 + (r & ~3) (a
+// 16-byte gap after every four rows), so 16-byte cp.async chunks stay aligned and the transposed reads of a warp
+// (16 columns x 2 rows) fall into 16 distinct banks.
+constexpr int SK_TILE = SK * SK + SK;  // floats per staged tile
+constexpr int SK_STAGES = 2;           // entries in flight per block: the next pair loads while this one computes
+constexpr int SK_SMEM = SK_STAGES * 2 * SK_TILE * (int)sizeof(float);
+PSGD_DEVI int sk_off(int r, int c) { return r * SK + (r & ~3) + c; }
+
+PSGD_DEVI void cp_async16(float* dst, const float* src, bool ok) {  // zero-fills dst when !ok (src not read)
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src), "r"(ok ? 16 : 0)
+               : "memory");
+}
+PSGD_DEVI void cp_async4(float* dst, const float* src, bool ok) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src), "r"(ok ? 4 : 0)
+               : "memory");
+}
+PSGD_DEVI void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+PSGD_DEVI void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Requests work entry w's tiles into one stage: A = Q[TI, TJ] at stage[0 ..), B = Q[TJ, TI] at stage[SK_TILE ..)
+// (not loaded on the diagonal, where B = A). Elements outside the matrix arrive as zeros. A warp covers two
+// 256-byte tile rows per request.
+PSGD_DEVI void skew_issue(const PsgdSkewItem* __restrict__ items, const uint32_t* __restrict__ work, int w,
+                          float* stage, int t) {
+  const PsgdSkewItem& it = items[work[2 * w]];
+  const int ti = work[2 * w + 1] >> 16, tj = work[2 * w + 1] & 0xFFFF;
+  const int n = it.n, i0 = ti * SK, j0 = tj * SK, nload = ti == tj ? 4 : 8;
+  const float* q = it.q;
+  const int c = 4 * (t & 15), r0 = t >> 4;
+  if ((n & 3) == 0 && (reinterpret_cast<uintptr_t>(q) & 15) == 0) {  // whole 16-byte chunks: each is inside the
+    // matrix or wholly outside
+    for (int j = 0; j < nload; ++j) {
+      const int tile = j >> 2, r = r0 + 16 * (j & 3);
+      const int gr = (tile ? j0 : i0) + r, gc = (tile ? i0 : j0) + c;
+      const bool ok = gr < n && gc < n;
+      cp_async16(stage + tile * SK_TILE + sk_off(r, c), ok ? q + (long long)gr * n + gc : q, ok);
+    }
+  } else {
+    for (int j = 0; j < nload; ++j) {
+      const int tile = j >> 2, r = r0 + 16 * (j & 3);
+      const int gr = (tile ? j0 : i0) + r, gc = (tile ? i0 : j0) + c;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const bool ok = gr < n && gc + e < n;
+        cp_async4(stage + tile * SK_TILE + sk_off(r, c + e), ok ? q + (long long)gr * n + gc + e : q, ok);
+      }
+    }
+  }
+}
+
 // R1: the items carry the rank-one q update (u_hi != NULL); without it that code is compiled out, so the plain
-// kernel keeps its register count and occupancy.
+// kernel keeps its register count. Entries of a block are pipelined through SK_STAGES shared-memory stages
+// (cp.async): entry k + SK_STAGES is requested as soon as entry k's tiles have been read.
 template <bool R1>
-__global__ void __launch_bounds__(256, R1 ? 3 : 4) skew_kernel(const PsgdSkewItem* __restrict__ items,
-                                                              const uint32_t* __restrict__ work, int nwork) {
-  __shared__ float sA[SK][SK + 1], sB[SK][SK + 1];
+__global__ void __launch_bounds__(256, 3) skew_kernel(const PsgdSkewItem* __restrict__ items,
+                                                      const uint32_t* __restrict__ work, int nwork) {
+  extern __shared__ __align__(16) float sk_stage[];
   __shared__ float red[8][2];
   // R1: u at the rows of A (i0 ..) and of B (j0 ..), v at the columns of A (j0 ..) and of B (i0 ..); hi and lo
   __shared__ float suv[R1 ? 4 : 1][2][SK];
   const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
   const int rr = t >> 4, c4 = (t & 15) * 4;  // this thread: rows rr + 16 m, columns c4 .. c4 + 3 of a tile
-  for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
+  int wnext = blockIdx.x;
+  for (int st = 0; st < SK_STAGES; ++st, wnext += gridDim.x) {
+    if (wnext < nwork) skew_issue(items, work, wnext, sk_stage + st * 2 * SK_TILE, t);
+    cp_async_commit();
+  }
+  int st = 0;
+  for (int w = blockIdx.x; w < nwork; w += gridDim.x, wnext += gridDim.x, st = st + 1 == SK_STAGES ? 0 : st + 1) {
     const PsgdSkewItem& it = items[work[2 * w]];
     const int ti = work[2 * w + 1] >> 16, tj = work[2 * w + 1] & 0xFFFF;
     const int n = it.n, i0 = ti * SK, j0 = tj * SK;
     const bool diag = ti == tj;
-    const bool vec = (n % 4) == 0;
+    const bool vec = (n % 4) == 0 && (reinterpret_cast<uintptr_t>(it.q) & 15) == 0;
+    float* const sA = sk_stage + st * 2 * SK_TILE;
+    float* const sB = diag ? sA : sA + SK_TILE;
+    const bool r1 = R1 && it.u_hi != nullptr;
+    if (r1) {  // the four 64-element segments of u and v this pair uses, one element per thread
+      const int seg = t >> 6, e = t & 63;
+      const int base = (seg == 0 || seg == 3) ? i0 : j0;
+      const int idx = min(base + e, n - 1);
+      const void* h = seg < 2 ? it.u_hi : it.v_hi;
+      const void* l = seg < 2 ? it.u_lo : it.v_lo;
+      const long long ld = seg < 2 ? it.ldu : it.ldv;
+      suv[seg][0][e] = ldbf(h, (long long)idx * ld);
+      suv[seg][1][e] = l ? ldbf(l, (long long)idx * ld) : 0.f;
+    }
+    cp_async_wait<SK_STAGES - 1>();  // this entry's group is complete (later groups may still be in flight)
+    __syncthreads();
     float4 a[4], b[4];  // this thread's rows of A and B: the untransposed operands of the differences below
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
-      a[m] = load4q(it.q, n, i0 + rr + 16 * m, j0 + c4, vec);
-      b[m] = diag ? a[m] : load4q(it.q, n, j0 + rr + 16 * m, i0 + c4, vec);
+      a[m] = *reinterpret_cast<const float4*>(sA + sk_off(rr + 16 * m, c4));
+      b[m] = *reinterpret_cast<const float4*>(sB + sk_off(rr + 16 * m, c4));
     }
-    const bool r1 = R1 && it.u_hi != nullptr;
     if (r1) {  // the rank-one q update of this pair of tiles, written back before Rn is formed from it
-      {  // the four 64-element segments of u and v this pair uses, one element per thread
-        const int seg = t >> 6, e = t & 63;
-        const int base = (seg == 0 || seg == 3) ? i0 : j0;
-        const int idx = min(base + e, n - 1);
-        const void* h = seg < 2 ? it.u_hi : it.v_hi;
-        const void* l = seg < 2 ? it.u_lo : it.v_lo;
-        const long long ld = seg < 2 ? it.ldu : it.ldv;
-        suv[seg][0][e] = ldbf(h, (long long)idx * ld);
-        suv[seg][1][e] = l ? ldbf(l, (long long)idx * ld) : 0.f;
-      }
-      __syncthreads();
       const float al = *it.alpha, be = *it.beta;
       float vha[4], vla[4], vhb[4], vlb[4];  // v at A's columns j0 + c4 + k and at B's columns i0 + c4 + k
 #pragma unroll
@@ -508,29 +573,19 @@ __global__ void __launch_bounds__(256, R1 ? 3 : 4) skew_kernel(const PsgdSkewIte
         a[m] = make_float4(xa[0], xa[1], xa[2], xa[3]);
         b[m] = diag ? a[m] : make_float4(xb[0], xb[1], xb[2], xb[3]);
         store4q(it.q, n, ia, j0 + c4, vec, a[m]);
-        if (!diag) store4q(it.q, n, ib, i0 + c4, vec, b[m]);
+        *reinterpret_cast<float4*>(sA + sk_off(rr + 16 * m, c4)) = a[m];
+        if (!diag) {
+          store4q(it.q, n, ib, i0 + c4, vec, b[m]);
+          *reinterpret_cast<float4*>(sB + sk_off(rr + 16 * m, c4)) = b[m];
+        }
       }
+      __syncthreads();
     }
-    {
-#pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const int r = rr + 16 * m;
-        sA[r][c4] = a[m].x;
-        sA[r][c4 + 1] = a[m].y;
-        sA[r][c4 + 2] = a[m].z;
-        sA[r][c4 + 3] = a[m].w;
-        sB[r][c4] = b[m].x;
-        sB[r][c4 + 1] = b[m].y;
-        sB[r][c4 + 2] = b[m].z;
-        sB[r][c4 + 3] = b[m].w;
-      }
-    }
-    __syncthreads();
     float mx = 0.f, dsum = 0.f;
     const int tiles32 = (n + 31) / 32;
     for (int half = 0; half < (diag ? 1 : 2); ++half) {
       // half 0: Rn[TI, TJ] rows i0 + r = A[r][c] - B[c][r]; half 1: Rn[TJ, TI] rows j0 + r = B[r][c] - A[c][r]
-      const float(*Y)[SK + 1] = half == 0 ? sB : sA;
+      const float* Y = half == 0 ? sB : sA;
       const int gr0 = half == 0 ? i0 : j0, gj0 = (half == 0 ? j0 : i0) + c4;
       const int slot = 2 * (half == 0 ? tj : ti);
       const int nv = max(0, min(4, n - gj0));
@@ -540,21 +595,20 @@ __global__ void __launch_bounds__(256, R1 ? 3 : 4) skew_kernel(const PsgdSkewIte
         const int r = rr + 16 * m, gi = gr0 + r;
         const float4 xv = half == 0 ? a[m] : b[m];
         const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
-        float v[4], rs = 0.f;
+        float yv[4], v[4], rs = 0.f;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const bool ok = gi < n && gj0 + k < n;
           const float x = xs[k];
-          v[k] = ok ? x - Y[c4 + k][r] : 0.f;
+          yv[k] = Y[sk_off(c4 + k, r)];
+          v[k] = ok ? x - yv[k] : 0.f;
           rs += v[k] * v[k];
           mx = fmaxf(mx, fabsf(v[k]));
           dsum += v[k] * x;
         }
         if (gi < n && nv > 0) st4_split(it.r_hi, it.r_lo, (long long)gi * it.ldr + gj0, v, vs, nv);
-        if (r1 && gi < n && nv > 0) {  // q^T of the updated q: its row gi is the transposed operand read above
-          const float yv[4] = {Y[c4][r], Y[c4 + 1][r], Y[c4 + 2][r], Y[c4 + 3][r]};
+        if (r1 && gi < n && nv > 0)  // q^T of the updated q: its row gi is the transposed operand read above
           st4_split(it.qt_hi, it.qt_lo, (long long)gi * it.ldqt + gj0, yv, nv == 4 && (it.ldqt % 4) == 0, nv);
-        }
         rs += __shfl_xor_sync(0xffffffffu, rs, 1);
         rs += __shfl_xor_sync(0xffffffffu, rs, 2);
         rs += __shfl_xor_sync(0xffffffffu, rs, 4);
@@ -568,7 +622,9 @@ __global__ void __launch_bounds__(256, R1 ? 3 : 4) skew_kernel(const PsgdSkewIte
       red[wid][0] = mx;
       red[wid][1] = dsum;
     }
-    __syncthreads();
+    __syncthreads();  // every thread is done with this stage: refill it
+    if (wnext < nwork) skew_issue(items, work, wnext, sA, t);
+    cp_async_commit();
     if (t == 0) {
       float m = 0.f, d = 0.f;
       for (int k = 0; k < 8; ++k) {
@@ -578,8 +634,8 @@ __global__ void __launch_bounds__(256, R1 ? 3 : 4) skew_kernel(const PsgdSkewIte
       it.part_max[(long long)(2 * ti) * tiles32 + 2 * tj] = m;
       it.part_dot[(long long)(2 * ti) * tiles32 + 2 * tj] = d;
     }
-    __syncthreads();
   }
+  cp_async_wait<0>();
 }
 
 // ---- M = a Rn / s + a^2 / 2 (S / s) / s ----------------------------------------------------------------------------
@@ -814,16 +870,30 @@ __global__ void __launch_bounds__(256) balance_apply_kernel(const PsgdBalanceFac
 // Grid of a grid-stride kernel: every block resident at once (SMs x the blocks per SM that the kernel's registers
 // and shared memory allow), so no second partial wave runs its share of the work alone at the end.
 template <typename Kernel>
-static int grid_for(Kernel kernel, int threads, int nwork) {
+static int grid_for(Kernel kernel, int threads, int nwork, int smem = 0) {
   int dev = 0, sms = 148, per_sm = 1;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0) != cudaSuccess || per_sm < 1)
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess || per_sm < 1)
     per_sm = 1;
   const int cap = sms * per_sm;
   return nwork < cap ? nwork : cap;
 }
 
 static int launched() { return cudaGetLastError() == cudaSuccess ? PSGD_OK : PSGD_ELAUNCH; }
+
+// Raises the skew kernel's dynamic shared-memory limit once per device (before any graph capture that uses it).
+template <bool R1>
+static bool skew_smem_attr() {
+  static bool done[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  if (!done[dev]) {
+    if (cudaFuncSetAttribute(skew_kernel<R1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM) != cudaSuccess)
+      return false;
+    done[dev] = true;
+  }
+  return true;
+}
 
 }  // namespace psgd
 
@@ -856,7 +926,8 @@ extern "C" int psgd_skew(const PsgdSkewItem* items, const uint32_t* work, int nw
                          cudaStream_t stream) {
   if (!items || !work || nwork < 0) return PSGD_EINVAL;
   if (nwork == 0) return PSGD_OK;
-  skew_kernel<false><<<grid_for(skew_kernel<false>, 256, nwork), 256, 0, stream>>>(items, work, nwork);
+  if (!skew_smem_attr<false>()) return PSGD_ELAUNCH;
+  skew_kernel<false><<<grid_for(skew_kernel<false>, 256, nwork, SK_SMEM), 256, SK_SMEM, stream>>>(items, work, nwork);
   return launched();
 }
 
@@ -864,7 +935,8 @@ extern "C" int psgd_skew_rank1(const PsgdSkewItem* items, const uint32_t* work, 
                                cudaStream_t stream) {
   if (!items || !work || nwork < 0) return PSGD_EINVAL;
   if (nwork == 0) return PSGD_OK;
-  skew_kernel<true><<<grid_for(skew_kernel<true>, 256, nwork), 256, 0, stream>>>(items, work, nwork);
+  if (!skew_smem_attr<true>()) return PSGD_ELAUNCH;
+  skew_kernel<true><<<grid_for(skew_kernel<true>, 256, nwork, SK_SMEM), 256, SK_SMEM, stream>>>(items, work, nwork);
   return launched();
 }
 
