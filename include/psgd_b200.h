@@ -127,9 +127,9 @@ int psgd_num_sms(void);
 /* Damping noise (items with xi != NULL): read from xi, or, when hyper[PSGD_HY_NOISE] != 0, generated in the kernel:
  * element e (index i * n2 + j of the item) gets the standard normal number s = noise_base + e of the sequence
  * Philox4x32-10 (Salmon et al., SC'11) with key (KEY0, KEY1) and counter (s / 4, 0, 0, 0), its four words w
- * taken as uniforms u = (w + 1/2) / 2^32 and two Box-Muller pairs: sqrt(-2 ln u0) (cos, sin)(2 pi u1 - pi) give
- * numbers 4c, 4c + 1, and words 2, 3 the same way give 4c + 2, 4c + 3. The values depend on the key and position
- * only, not on the launch geometry. */
+ * taken as uniforms u = ((w >> 9) + 1/2) / 2^23 and two Box-Muller pairs: sqrt(-2 ln u0) (cos, sin)(2 pi u1 - pi)
+ * give numbers 4c, 4c + 1, and words 2, 3 the same way give 4c + 2, 4c + 3. The values depend on the key and
+ * position only, not on the launch geometry. */
 #define PSGD_PREP_NORMAL 0
 #define PSGD_PREP_TRANS 1
 #define PSGD_PREP_DIRECT 2

@@ -13,7 +13,6 @@ namespace psgd {
 constexpr int TT = 32;        // tile edge of the tiled element-wise kernels
 constexpr int TROWS = 8;      // threads per tile column (256 threads, 4 rows each)
 constexpr int PREP_ROWS = PSGD_PREP_ROWS;  // rows per work entry of the row-vector staging path
-constexpr int PREP_SUB = 4;                // rows a thread stages at once (loads in flight)
 
 PSGD_DEVI float load_g(const void* g, int bf16, long long idx) {
   return bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(g)[idx])
@@ -51,14 +50,17 @@ PSGD_DEVI uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {
 }
 
 // Numbers 4 blk .. 4 blk + 3 of the sequence with key (k0, k1).
+PSGD_DEVI float unit_open(uint32_t w) {  // ((w >> 9) + 1/2) / 2^23, exactly: [1, 2) by its bits, minus 1 - 2^-24
+  return __uint_as_float(0x3f800000u | (w >> 9)) - 0.99999994039535522f;
+}
 PSGD_DEVI float4 normal4(unsigned long long blk, uint32_t k0, uint32_t k1) {
   const uint4 w = philox4x32_10(make_uint4((uint32_t)blk, (uint32_t)(blk >> 32), 0u, 0u), k0, k1);
-  constexpr float inv32 = 2.3283064365386963e-10f;  // 2^-32: uniforms (w + 1/2) / 2^32 in (0, 1)
-  const float u0 = ((float)w.x + 0.5f) * inv32, u1 = ((float)w.y + 0.5f) * inv32;
-  const float u2 = ((float)w.z + 0.5f) * inv32, u3 = ((float)w.w + 0.5f) * inv32;
-  // hardware approximations of log, sin and cos (errors near 1e-6, far below what damping noise needs); the
-  // angle 2 pi u - pi lies in [-pi, pi), where __sincosf is most accurate
-  const float r0 = sqrtf(-2.f * __logf(u0)), r1 = sqrtf(-2.f * __logf(u2));
+  const float u0 = unit_open(w.x), u1 = unit_open(w.y), u2 = unit_open(w.z), u3 = unit_open(w.w);
+  // hardware approximations of log, reciprocal square root, sin and cos (errors near 1e-6, far below what damping
+  // noise needs); -2 ln u > 0 for every u above; the angle 2 pi u - pi lies in (-pi, pi), where __sincosf is most
+  // accurate
+  const float t0 = -2.f * __logf(u0), t2 = -2.f * __logf(u2);
+  const float r0 = t0 * rsqrtf(t0), r1 = t2 * rsqrtf(t2);
   constexpr float TWO_PI = 6.2831853071795865f, PI = 3.1415926535897932f;
   float s0, c0, s1, c1;
   __sincosf(TWO_PI * u1 - PI, &s0, &c0);
@@ -74,9 +76,79 @@ PSGD_DEVI float normal1(unsigned long long s, uint32_t k0, uint32_t k1) {
 }
 
 // ---- gradient staging ------------------------------------------------------------------------------------------
+// PREP_NORMAL rows r0 .. r0 + rows - 1 in 8-element vectors (16-byte bf16 G chunks, two for fp32 G; 16-byte
+// operand stores). Each thread first requests PREP_VEC vectors' G chunks into its own shared-memory slots
+// (cp.async: the loads are in flight together without holding registers), then converts them one at a time.
+constexpr int PREP_VEC = 8;                                     // bf16 G vectors per thread per batch (fp32: half)
+constexpr int PREP_SMEM = PREP_VEC * 256 * (int)sizeof(uint4);  // 32 KB: a thread's slots at stage[s * 256 + t]
+
+PSGD_DEVI void cp_async16_raw(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src)
+               : "memory");
+}
+
+template <bool BF16>
+PSGD_DEVI void prep_rows_vec8(const PsgdPrepItem& it, long long r0, int rows, float damping, bool gen, uint32_t k0,
+                              uint32_t k1, uint4* stage) {
+  constexpr int PV = BF16 ? PREP_VEC : PREP_VEC / 2, CH = BF16 ? 1 : 2;  // vectors per batch, chunks per vector
+  const int nvr = it.n2 >> 3, nvec = rows * nvr, t = threadIdx.x;
+  for (int base = t; base < nvec; base += blockDim.x * PV) {
+#pragma unroll
+    for (int s = 0; s < PV; ++s) {
+      const int j = base + s * blockDim.x;
+      if (j < nvec) {
+        const int r = j / nvr;
+        const long long idx = (r0 + r) * it.n2 + (long long)(j - r * nvr) * 8;
+        const char* src = reinterpret_cast<const char*>(it.g) + idx * (BF16 ? 2 : 4);
+#pragma unroll
+        for (int c = 0; c < CH; ++c) cp_async16_raw(stage + (s * CH + c) * 256 + t, src + 16 * c);
+      }
+    }
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
+#pragma unroll 1
+    for (int s = 0; s < PV; ++s) {
+      const int j = base + s * blockDim.x;
+      if (j >= nvec) break;
+      const int r = j / nvr;
+      const long long row = r0 + r, col = (long long)(j - r * nvr) * 8, idx = row * it.n2 + col;
+      float x[8];
+      if (BF16) {
+        const uint4 v = stage[s * 256 + t];
+        const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = __bfloat162float(h[i]);
+      } else {
+        const float4 a = reinterpret_cast<const float4*>(stage)[(2 * s) * 256 + t];
+        const float4 b = reinterpret_cast<const float4*>(stage)[(2 * s + 1) * 256 + t];
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+        x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+      }
+      if (it.xi) {
+#pragma unroll
+        for (int hv = 0; hv < 2; ++hv) {
+          const float4 z = gen ? normal4((unsigned long long)(it.noise_base + idx) / 4 + hv, k0, k1)
+                               : *reinterpret_cast<const float4*>(it.xi + idx + 4 * hv);
+          const float zz[4] = {z.x, z.y, z.z, z.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) x[4 * hv + i] += (damping + it.eps * fabsf(x[4 * hv + i])) * zz[i];
+        }
+      }
+      __align__(16) __nv_bfloat16 h[8], l[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) split_bf16(x[i], h[i], l[i]);
+      const long long o = row * it.ld_out + col;
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(it.out_hi) + o) = *reinterpret_cast<const uint4*>(h);
+      if (it.out_lo)
+        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(it.out_lo) + o) = *reinterpret_cast<const uint4*>(l);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(256) prep_kernel(const PsgdPrepItem* __restrict__ items,
                                                   const uint32_t* __restrict__ work, int nwork,
                                                   const float* __restrict__ hyper) {
+  extern __shared__ uint4 prep_stage[];  // PREP_SMEM bytes: the row-vector path's G slots
   __shared__ float tile[TT][TT + 1];
   __shared__ float colred[TROWS][TT];
   __shared__ float tred[TROWS];
@@ -89,53 +161,16 @@ __global__ void __launch_bounds__(256) prep_kernel(const PsgdPrepItem* __restric
     if (it.mode == PSGD_PREP_NORMAL) {  // rows PREP_ROWS * wv .. : 4-element vectors along each row
       const long long r0 = (long long)work[2 * w + 1] * PREP_ROWS;
       const int rows = (int)min((long long)PREP_ROWS, it.n1 - r0);
-      const bool vec = (it.n2 % 4) == 0 &&
-                       ((reinterpret_cast<uintptr_t>(it.g) & (it.g_bf16 ? 7 : 15)) == 0) &&
+      const bool vec = (it.n2 % 8) == 0 && (reinterpret_cast<uintptr_t>(it.g) & 15) == 0 &&
                        (it.xi == nullptr || (reinterpret_cast<uintptr_t>(it.xi) & 15) == 0) &&
-                       (it.noise_base & 3) == 0;
+                       (it.noise_base & 3) == 0 && (it.ld_out % 8) == 0 &&
+                       (reinterpret_cast<uintptr_t>(it.out_hi) & 15) == 0 &&
+                       (reinterpret_cast<uintptr_t>(it.out_lo) & 15) == 0;
       if (vec) {
-        // one 4-column vector per thread across PREP_SUB rows at a time: PREP_SUB gradient loads in flight per
-        // thread, no index divisions
-        const int nv = it.n2 / 4;
-        for (int kv = threadIdx.x; kv < nv; kv += blockDim.x) {
-          const long long col = (long long)kv * 4;
-          for (int rs = 0; rs < rows; rs += PREP_SUB) {
-            float x[PREP_SUB][4];
-#pragma unroll
-            for (int r = 0; r < PREP_SUB; ++r) {
-              if (rs + r >= rows) break;
-              const long long idx = (r0 + rs + r) * it.n2 + col;
-              if (it.g_bf16) {
-                const uint2 gv = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(it.g) + idx);
-                const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&gv);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) x[r][i] = __bfloat162float(h[i]);
-              } else {
-                const float4 v = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(it.g) + idx);
-                x[r][0] = v.x; x[r][1] = v.y; x[r][2] = v.z; x[r][3] = v.w;
-              }
-            }
-#pragma unroll
-            for (int r = 0; r < PREP_SUB; ++r) {
-              if (rs + r >= rows) break;
-              const long long row = r0 + rs + r, idx = row * it.n2 + col;
-              if (it.xi) {
-                const float4 z = gen ? normal4((unsigned long long)(it.noise_base + idx) >> 2, k0, k1)
-                                     : *reinterpret_cast<const float4*>(it.xi + idx);
-                const float zz[4] = {z.x, z.y, z.z, z.w};
-#pragma unroll
-                for (int i = 0; i < 4; ++i) x[r][i] += (damping + it.eps * fabsf(x[r][i])) * zz[i];
-              }
-              __align__(8) __nv_bfloat16 h[4], l[4];
-#pragma unroll
-              for (int i = 0; i < 4; ++i) split_bf16(x[r][i], h[i], l[i]);
-              const long long o = row * it.ld_out + col;
-              *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(it.out_hi) + o) = *reinterpret_cast<const uint2*>(h);
-              if (it.out_lo)
-                *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(it.out_lo) + o) = *reinterpret_cast<const uint2*>(l);
-            }
-          }
-        }
+        if (it.g_bf16)
+          prep_rows_vec8<true>(it, r0, rows, damping, gen, k0, k1, prep_stage);
+        else
+          prep_rows_vec8<false>(it, r0, rows, damping, gen, k0, k1, prep_stage);
       } else {
         for (int k = threadIdx.x; k < rows * it.n2; k += blockDim.x) {
           const long long row = r0 + k / it.n2, col = k % it.n2;
@@ -903,7 +938,7 @@ extern "C" int psgd_prep(const PsgdPrepItem* items, const uint32_t* work, int nw
                          cudaStream_t stream) {
   if (!items || !work || !hyper || nwork < 0) return PSGD_EINVAL;
   if (nwork == 0) return PSGD_OK;
-  prep_kernel<<<grid_for(prep_kernel, 256, nwork), 256, 0, stream>>>(items, work, nwork, hyper);
+  prep_kernel<<<grid_for(prep_kernel, 256, nwork, PREP_SMEM), 256, PREP_SMEM, stream>>>(items, work, nwork, hyper);
   return launched();
 }
 

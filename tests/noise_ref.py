@@ -1,6 +1,7 @@
 """Test-side restatement of the in-kernel damping-noise generator (psgd_prep with hyper[PSGD_HY_NOISE] set):
 Philox4x32-10 (Salmon, Moraes, Dror and Shaw, SC'11) on counter (s / 4, 0, 0, 0) with a 2-word key, the four words
-turned into four standard normal numbers by two Box-Muller transforms (angles 2 pi u - pi). numpy, float64 transforms."""
+turned into uniforms ((w >> 9) + 1/2) / 2^23 and four standard normal numbers by two Box-Muller transforms (angles
+2 pi u - pi). numpy, float64 transforms."""
 import numpy as np
 
 M0, M1, W0, W1 = 0xD2511F53, 0xCD9E8D57, 0x9E3779B9, 0xBB67AE85
@@ -27,8 +28,8 @@ def normals(positions, k0, k1):
     pos = np.asarray(positions, dtype=np.uint64)
     blk = pos >> np.uint64(2)
     c = np.stack([blk & np.uint64(MASK), blk >> np.uint64(32), np.zeros_like(blk), np.zeros_like(blk)], axis=-1)
-    w = philox4x32_10(c, (k0, k1)).astype(np.float64)
-    u = (w + 0.5) * 2.0 ** -32
+    w = philox4x32_10(c, (k0, k1))
+    u = ((w >> np.uint64(9)).astype(np.float64) + 0.5) * 2.0 ** -23  # the top 23 bits of each word
     r0, r1 = np.sqrt(-2 * np.log(u[..., 0])), np.sqrt(-2 * np.log(u[..., 2]))
     t1, t3 = 2 * np.pi * u[..., 1] - np.pi, 2 * np.pi * u[..., 3] - np.pi
     z = np.stack([r0 * np.cos(t1), r0 * np.sin(t1), r1 * np.cos(t3), r1 * np.sin(t3)], axis=-1)

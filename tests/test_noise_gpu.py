@@ -14,13 +14,14 @@ from psgd_pro_b200 import kernels as K
 pytestmark = pytest.mark.gpu
 
 
-def staged_noise(dev, n1, n2, mode, base, key, split=True):
-    g = torch.zeros(n1, n2, device=dev)
+def staged_noise(dev, n1, n2, mode, base, key, split=True, g_dtype=torch.float32):
+    g = torch.zeros(n1, n2, device=dev, dtype=g_dtype)
     dummy = torch.zeros(4, device=dev)  # any non-null xi marks the item as one with damping noise
     rows, cols = (n2, n1) if mode == _capi.PSGD_PREP_TRANS else (n1, n2)
     hi, lo = K.operand(rows, cols, dev, split=split)
     it = _capi.PrepItem()
-    it.g, it.g_bf16, it.mode, it.xi, it.n1, it.n2 = g.data_ptr(), 0, mode, dummy.data_ptr(), n1, n2
+    it.g, it.g_bf16 = g.data_ptr(), int(g_dtype == torch.bfloat16)
+    it.mode, it.xi, it.n1, it.n2 = mode, dummy.data_ptr(), n1, n2
     it.out_hi, it.out_lo, it.ld_out, it.eps, it.noise_base = K.ptr(hi), K.ptr(lo), hi.stride(0), 0.0, base
     host = torch.empty(ctypes.sizeof(it), dtype=torch.uint8)
     ctypes.memmove(host.data_ptr(), ctypes.addressof(it), ctypes.sizeof(it))
@@ -52,6 +53,8 @@ def test_noise_matches_reference(cuda, n1, n2, base):
     assert np.abs(z - want).max() < 2e-4 * max(1.0, np.abs(want).max())
     zt = staged_noise(cuda, n1, n2, _capi.PSGD_PREP_TRANS, base, key)  # another launch geometry: same numbers
     assert np.abs(zt.T - z).max() < 1e-6 * max(1.0, np.abs(z).max())
+    zb = staged_noise(cuda, n1, n2, _capi.PSGD_PREP_NORMAL, base, key, g_dtype=torch.bfloat16)  # bf16 G path
+    assert np.array_equal(zb, z)
 
 
 def test_noise_keys_and_moments(cuda):
