@@ -134,13 +134,21 @@ PSGD_DEVI void prep_rows_vec8(const PsgdPrepItem& it, long long r0, int rows, fl
           for (int i = 0; i < 4; ++i) x[4 * hv + i] += (damping + it.eps * fabsf(x[4 * hv + i])) * zz[i];
         }
       }
-      __align__(16) __nv_bfloat16 h[8], l[8];
+      // hi = bf16(x) two at a time (packed conversions); lo = bf16(x - hi) only when the item stages lo halves
+      __align__(16) __nv_bfloat162 h[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) split_bf16(x[i], h[i], l[i]);
+      for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
       const long long o = row * it.ld_out + col;
       *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(it.out_hi) + o) = *reinterpret_cast<const uint4*>(h);
-      if (it.out_lo)
+      if (it.out_lo) {
+        __align__(16) __nv_bfloat162 l[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 hf = __bfloat1622float2(h[i]);
+          l[i] = __floats2bfloat162_rn(x[2 * i] - hf.x, x[2 * i + 1] - hf.y);
+        }
         *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(it.out_lo) + o) = *reinterpret_cast<const uint4*>(l);
+      }
     }
   }
 }
