@@ -162,8 +162,8 @@ typedef struct PsgdNlbPrepItem {
 } PsgdNlbPrepItem;
 int psgd_nlb_prep(const PsgdNlbPrepItem* items, int nitems, int* dev_err, cudaStream_t stream);
 
-/* Per-factor scalar work after the subspace iteration, one CTA per item (psgd_pro.py:126-135,
- * psgd_pro_fast.py:178-189):
+/* Per-factor scalar work after the subspace iteration (psgd_pro.py:126-135, psgd_pro_fast.py:178-189); one CTA
+ * per item, except FACTOR_DIAG items, whose n entries are split into PSGD_FAC_SPLIT ranges (two launches):
  *   FACTOR_DENSE: ell = nf * max_c sqrt(sum_t part[t * ncols + c]) + term2  (the bound of the 4th product)
  *   FACTOR_RANK1: ell = sum_t part[t] + term2                  (1-D gradient: term1 = Pg Pg^T, bound = |Pg|^2)
  *   both: L = max(betaL L + (1 - betaL) ell, ell); *alpha = -lr/L; *beta = 1 + lr/L * term2
@@ -185,7 +185,10 @@ typedef struct PsgdFactorItem {
   float* q; float* p;
   const float* part_dot_rq; int n_rq;
   const float* part_dot_sq; int n_sq;
+  float* scratch;  /* FACTOR_DIAG: PSGD_FAC_SCRATCH floats (the item's n is split into PSGD_FAC_SPLIT ranges) */
 } PsgdFactorItem;
+#define PSGD_FAC_SPLIT 16
+#define PSGD_FAC_SCRATCH 32
 int psgd_factor_update(const PsgdFactorItem* items, int nitems, const float* hyper, int* dev_err,
                        cudaStream_t stream);
 

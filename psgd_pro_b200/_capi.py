@@ -54,7 +54,7 @@ class NlbPrepItem(ctypes.Structure):
 class FactorItem(ctypes.Structure):
     _fields_ = [("kind", c_int), ("n", c_int), ("term2", c_float), ("L", c_vp), ("nf", c_vp), ("part", c_vp),
                 ("slots", c_int), ("ncols", c_int), ("alpha", c_vp), ("beta", c_vp), ("q", c_vp), ("p", c_vp),
-                ("part_dot_rq", c_vp), ("n_rq", c_int), ("part_dot_sq", c_vp), ("n_sq", c_int)]
+                ("part_dot_rq", c_vp), ("n_rq", c_int), ("part_dot_sq", c_vp), ("n_sq", c_int), ("scratch", c_vp)]
 
 
 class SkewItem(ctypes.Structure):
@@ -88,6 +88,7 @@ PSGD_PREP_NORMAL, PSGD_PREP_TRANS, PSGD_PREP_DIRECT = 0, 1, 2
 PREP_ROWS = 8
 ROT_ROWS = 8
 SKEW_TILE = 64
+FAC_SCRATCH = 32   # floats of scratch per diagonal factor item
 PSGD_FACTOR_DENSE, PSGD_FACTOR_RANK1, PSGD_FACTOR_DIAG, PSGD_FACTOR_SKEW = 0, 1, 2, 3
 HY_LR_PRECOND, HY_BETA_L, HY_DAMPING, HY_LR_PARAMS, HY_MAX_AVG, HY_MAX_ELEM, HY_MOM_BETA = range(7)
 HY_NOISE, HY_NOISE_KEY0, HY_NOISE_KEY1, HY_COUNT = 7, 8, 9, 12

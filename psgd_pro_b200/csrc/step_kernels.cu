@@ -328,6 +328,13 @@ __global__ void __launch_bounds__(NLB_THREADS) nlb_prep_kernel(const PsgdNlbPrep
   }
 }
 
+// Range c of nsplit ranges of 0 .. n (multiples of 32 long; empty past the end).
+PSGD_DEVI void split_range(int n, int nsplit, int c, int& lo, int& hi) {
+  const int ch = ((n + nsplit - 1) / nsplit + 31) & ~31;
+  lo = min(n, c * ch);
+  hi = min(n, lo + ch);
+}
+
 // ---- per-factor scalars ------------------------------------------------------------------------------------------
 constexpr int FAC_THREADS = 256;
 
@@ -364,9 +371,15 @@ PSGD_DEVI float max_col_norm(const float* part, int slots, int ncols, float* red
   return block_max(m, red);
 }
 
+// Blocks item * FAC_SPLIT + c: FACTOR_DIAG items use every c (ranges of their n entries), the others c = 0 only.
+constexpr int FAC_SPLIT = PSGD_FAC_SPLIT;
+static_assert(FAC_SPLIT + 1 <= PSGD_FAC_SCRATCH, "factor scratch too small");
+
 __global__ void __launch_bounds__(FAC_THREADS) factor_kernel(const PsgdFactorItem* __restrict__ items,
                                                             const float* __restrict__ hyper) {
-  const PsgdFactorItem& it = items[blockIdx.x];
+  const PsgdFactorItem& it = items[blockIdx.x / FAC_SPLIT];
+  const int c = blockIdx.x % FAC_SPLIT;
+  if (c != 0 && it.kind != PSGD_FACTOR_DIAG) return;
   __shared__ float red[FAC_THREADS / 32];
   const float lr = hyper[PSGD_HY_LR_PRECOND], betaL = hyper[PSGD_HY_BETA_L];
   if (it.kind == PSGD_FACTOR_DENSE || it.kind == PSGD_FACTOR_RANK1) {
@@ -386,27 +399,21 @@ __global__ void __launch_bounds__(FAC_THREADS) factor_kernel(const PsgdFactorIte
       *it.alpha = -coef;
       *it.beta = 1.f + coef * it.term2;
     }
-  } else if (it.kind == PSGD_FACTOR_DIAG) {
-    const int n = it.n;
+  } else if (it.kind == PSGD_FACTOR_DIAG) {  // this range's term1 (kept in p until factor_diag_kernel) and max
+    int lo, hi;
+    split_range(it.n, FAC_SPLIT, c, lo, hi);
     float m = -FLT_MAX;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
       float t1 = 0.f;
-      for (int s = 0; s < it.slots; ++s) t1 += it.part[(long long)s * n + i];
+      for (int s = 0; s < it.slots; ++s) t1 += it.part[(long long)s * it.n + i];
+      it.p[i] = t1;
       m = fmaxf(m, t1);
     }
-    const float ell = block_max(m, red) + it.term2;
-    const float Lold = *it.L;
-    const float L = fmaxf(betaL * Lold + (1.f - betaL) * ell, ell);
-    const float coef = lr / L;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      float t1 = 0.f;
-      for (int s = 0; s < it.slots; ++s) t1 += it.part[(long long)s * n + i];
-      const float q = it.q[i] * (1.f - coef * (t1 - it.term2));
-      it.q[i] = q;
-      it.p[i] = q * q;
+    m = block_max(m, red);
+    if (threadIdx.x == 0) {
+      it.scratch[c] = m;
+      if (c == 0) it.scratch[FAC_SPLIT] = *it.L;
     }
-    __syncthreads();
-    if (threadIdx.x == 0) *it.L = L;
   } else {  // PSGD_FACTOR_SKEW
     const float s = *it.nf * max_col_norm(it.part, it.slots, it.ncols, red) + FLT_MIN;
     float a1 = 0.f;
@@ -426,6 +433,29 @@ __global__ void __launch_bounds__(FAC_THREADS) factor_kernel(const PsgdFactorIte
       *it.beta = 1.f / s;
     }
   }
+}
+
+// FACTOR_DIAG, second launch: ell = max term1 + term2 over the ranges, L and the update of q and p in this range.
+__global__ void __launch_bounds__(FAC_THREADS) factor_diag_kernel(const PsgdFactorItem* __restrict__ items,
+                                                                 const float* __restrict__ hyper) {
+  const PsgdFactorItem& it = items[blockIdx.x / FAC_SPLIT];
+  if (it.kind != PSGD_FACTOR_DIAG) return;
+  const int c = blockIdx.x % FAC_SPLIT;
+  const float lr = hyper[PSGD_HY_LR_PRECOND], betaL = hyper[PSGD_HY_BETA_L];
+  float m = it.scratch[0];
+  for (int k = 1; k < FAC_SPLIT; ++k) m = fmaxf(m, it.scratch[k]);
+  const float ell = m + it.term2;
+  const float Lold = it.scratch[FAC_SPLIT];
+  const float L = fmaxf(betaL * Lold + (1.f - betaL) * ell, ell);
+  const float coef = lr / L;
+  int lo, hi;
+  split_range(it.n, FAC_SPLIT, c, lo, hi);
+  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    const float q = it.q[i] * (1.f - coef * (it.p[i] - it.term2));
+    it.q[i] = q;
+    it.p[i] = q * q;
+  }
+  if (c == 0 && threadIdx.x == 0) *it.L = L;
 }
 
 // ---- Rn = Q - Q^T ------------------------------------------------------------------------------------------------
@@ -961,7 +991,8 @@ extern "C" int psgd_factor_update(const PsgdFactorItem* items, int nitems, const
                                   cudaStream_t stream) {
   if (!items || !hyper || nitems < 0) return PSGD_EINVAL;
   if (nitems == 0) return PSGD_OK;
-  factor_kernel<<<nitems, FAC_THREADS, 0, stream>>>(items, hyper);
+  factor_kernel<<<nitems * FAC_SPLIT, FAC_THREADS, 0, stream>>>(items, hyper);
+  factor_diag_kernel<<<nitems * FAC_SPLIT, FAC_THREADS, 0, stream>>>(items, hyper);
   return launched();
 }
 

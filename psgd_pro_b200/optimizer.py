@@ -322,6 +322,8 @@ class _Plan:
                 part, slots = self.t1[f.fidx]
                 it.kind, it.part, it.slots, it.q, it.p = PSGD_FACTOR_DIAG, part.data_ptr(), slots, f.q.data_ptr(), \
                     f.p.data_ptr()
+                f.fac_scratch = torch.zeros(_capi.FAC_SCRATCH, device=dev)
+                it.scratch = f.fac_scratch.data_ptr()
             it.alpha, it.beta = self.s(f, S_AQ).data_ptr(), self.s(f, S_BQ).data_ptr()
             fi.append(it)
         self.fac_dev, self.fac_n = _upload(_capi.FactorItem, fi, dev), len(fi)
@@ -588,9 +590,10 @@ class _Plan:
         n = 3  # prep, clip scale, apply
         groups = [self.g_a1, self.g_a2]
         if update:
-            n += 1 + 2 * int(self.nlb_spd_n > 0) + 2 + int(self.skew_n > 0) + int(self.skew1_n > 0)
-            n += int(self.skew_n + self.skew1_n > 0)  # prep, nlb preps, factor x2, skew (two kinds), rot
-            n -= int(self.skf_n == 0)
+            n += 1  # prep
+            n += int(self.nlb_spd_n > 0) + int(self.nlb_skh_n > 0)  # norm-bound starts
+            n += 2 * int(self.fac_n > 0) + 2 * int(self.skf_n > 0)  # factor scalars: two launches each
+            n += int(self.skew_n > 0) + int(self.skew1_n > 0) + int(self.rot_n > 0)  # skew (two kinds), rot
             groups += [self.g_u1, self.g_u2, self.g_u3, self.g_u3r, self.g_u10, self.g_u17, self.g_u20, self.g_u22]
             groups += self.g_spd + self.g_skh
         return n + sum(g is not None for g in groups)
