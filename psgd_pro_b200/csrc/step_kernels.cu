@@ -614,81 +614,96 @@ __global__ void __launch_bounds__(256, 3) skew_kernel(const PsgdSkewItem* __rest
       a[m] = *reinterpret_cast<const float4*>(sA + sk_off(rr + 16 * m, c4));
       b[m] = *reinterpret_cast<const float4*>(sB + sk_off(rr + 16 * m, c4));
     }
-    if (r1) {  // the rank-one q update of this pair of tiles, written back before Rn is formed from it
-      const float al = *it.alpha, be = *it.beta;
-      float vha[4], vla[4], vhb[4], vlb[4];  // v at A's columns j0 + c4 + k and at B's columns i0 + c4 + k
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        vha[k] = suv[2][0][c4 + k];
-        vla[k] = suv[2][1][c4 + k];
-        vhb[k] = suv[3][0][c4 + k];
-        vlb[k] = suv[3][1][c4 + k];
-      }
-#pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const int ia = i0 + rr + 16 * m, ib = j0 + rr + 16 * m;
-        const float uha = suv[0][0][rr + 16 * m], ula = suv[0][1][rr + 16 * m];
-        const float uhb = suv[1][0][rr + 16 * m], ulb = suv[1][1][rr + 16 * m];
-        float xa[4] = {a[m].x, a[m].y, a[m].z, a[m].w}, xb[4] = {b[m].x, b[m].y, b[m].z, b[m].w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          // the K = 1 product as the tensor cores form it (hi * hi, then + hi * lo, then + lo * hi), then the
-          // q-update epilogue: alpha * acc + beta * q
-          float acc = uha * vha[k];
-          acc = fmaf(uha, vla[k], acc);
-          acc = fmaf(ula, vha[k], acc);
-          xa[k] = (ia < n && j0 + c4 + k < n) ? fmaf(be, xa[k], acc * al) : 0.f;
-          float bcc = uhb * vhb[k];
-          bcc = fmaf(uhb, vlb[k], bcc);
-          bcc = fmaf(ulb, vhb[k], bcc);
-          xb[k] = (ib < n && i0 + c4 + k < n) ? fmaf(be, xb[k], bcc * al) : 0.f;
-        }
-        a[m] = make_float4(xa[0], xa[1], xa[2], xa[3]);
-        b[m] = diag ? a[m] : make_float4(xb[0], xb[1], xb[2], xb[3]);
-        store4q(it.q, n, ia, j0 + c4, vec, a[m]);
-        *reinterpret_cast<float4*>(sA + sk_off(rr + 16 * m, c4)) = a[m];
-        if (!diag) {
-          store4q(it.q, n, ib, i0 + c4, vec, b[m]);
-          *reinterpret_cast<float4*>(sB + sk_off(rr + 16 * m, c4)) = b[m];
-        }
-      }
-      __syncthreads();
-    }
     float mx = 0.f, dsum = 0.f;
     const int tiles32 = (n + 31) / 32;
-    for (int half = 0; half < (diag ? 1 : 2); ++half) {
-      // half 0: Rn[TI, TJ] rows i0 + r = A[r][c] - B[c][r]; half 1: Rn[TJ, TI] rows j0 + r = B[r][c] - A[c][r]
-      const float* Y = half == 0 ? sB : sA;
-      const int gr0 = half == 0 ? i0 : j0, gj0 = (half == 0 ? j0 : i0) + c4;
-      const int slot = 2 * (half == 0 ? tj : ti);
-      const int nv = max(0, min(4, n - gj0));
-      const bool vs = nv == 4 && (it.ldr % 4) == 0;
-#pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const int r = rr + 16 * m, gi = gr0 + r;
-        const float4 xv = half == 0 ? a[m] : b[m];
-        const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
-        float yv[4], v[4], rs = 0.f;
+    // FULL: both tiles lie inside the matrix and every access is a whole vector: no bounds tests per element
+    const bool full = vec && i0 + SK <= n && j0 + SK <= n && (it.ldr % 4) == 0 && (!r1 || (it.ldqt % 4) == 0);
+    auto body = [&](auto full_tag) {
+      constexpr bool FULL = decltype(full_tag)::value;
+      if (r1) {  // the rank-one q update of this pair of tiles, written back before Rn is formed from it
+        const float al = *it.alpha, be = *it.beta;
+        float vha[4], vla[4], vhb[4], vlb[4];  // v at A's columns j0 + c4 + k and at B's columns i0 + c4 + k
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const bool ok = gi < n && gj0 + k < n;
-          const float x = xs[k];
-          yv[k] = Y[sk_off(c4 + k, r)];
-          v[k] = ok ? x - yv[k] : 0.f;
-          rs += v[k] * v[k];
-          mx = fmaxf(mx, fabsf(v[k]));
-          dsum += v[k] * x;
+          vha[k] = suv[2][0][c4 + k];
+          vla[k] = suv[2][1][c4 + k];
+          vhb[k] = suv[3][0][c4 + k];
+          vlb[k] = suv[3][1][c4 + k];
         }
-        if (gi < n && nv > 0) st4_split(it.r_hi, it.r_lo, (long long)gi * it.ldr + gj0, v, vs, nv);
-        if (r1 && gi < n && nv > 0)  // q^T of the updated q: its row gi is the transposed operand read above
-          st4_split(it.qt_hi, it.qt_lo, (long long)gi * it.ldqt + gj0, yv, nv == 4 && (it.ldqt % 4) == 0, nv);
-        rs += __shfl_xor_sync(0xffffffffu, rs, 1);
-        rs += __shfl_xor_sync(0xffffffffu, rs, 2);
-        rs += __shfl_xor_sync(0xffffffffu, rs, 4);
-        rs += __shfl_xor_sync(0xffffffffu, rs, 8);
-        if ((t & 15) == 0 && gi < n) it.part_row[(long long)slot * n + gi] = rs;
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const int ia = i0 + rr + 16 * m, ib = j0 + rr + 16 * m;
+          const float uha = suv[0][0][rr + 16 * m], ula = suv[0][1][rr + 16 * m];
+          const float uhb = suv[1][0][rr + 16 * m], ulb = suv[1][1][rr + 16 * m];
+          float xa[4] = {a[m].x, a[m].y, a[m].z, a[m].w}, xb[4] = {b[m].x, b[m].y, b[m].z, b[m].w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            // the K = 1 product as the tensor cores form it (hi * hi, then + hi * lo, then + lo * hi), then the
+            // q-update epilogue: alpha * acc + beta * q
+            float acc = uha * vha[k];
+            acc = fmaf(uha, vla[k], acc);
+            acc = fmaf(ula, vha[k], acc);
+            xa[k] = (FULL || (ia < n && j0 + c4 + k < n)) ? fmaf(be, xa[k], acc * al) : 0.f;
+            float bcc = uhb * vhb[k];
+            bcc = fmaf(uhb, vlb[k], bcc);
+            bcc = fmaf(ulb, vhb[k], bcc);
+            xb[k] = (FULL || (ib < n && i0 + c4 + k < n)) ? fmaf(be, xb[k], bcc * al) : 0.f;
+          }
+          a[m] = make_float4(xa[0], xa[1], xa[2], xa[3]);
+          b[m] = diag ? a[m] : make_float4(xb[0], xb[1], xb[2], xb[3]);
+          if (FULL)
+            *reinterpret_cast<float4*>(it.q + (long long)ia * n + j0 + c4) = a[m];
+          else
+            store4q(it.q, n, ia, j0 + c4, vec, a[m]);
+          *reinterpret_cast<float4*>(sA + sk_off(rr + 16 * m, c4)) = a[m];
+          if (!diag) {
+            if (FULL)
+              *reinterpret_cast<float4*>(it.q + (long long)ib * n + i0 + c4) = b[m];
+            else
+              store4q(it.q, n, ib, i0 + c4, vec, b[m]);
+            *reinterpret_cast<float4*>(sB + sk_off(rr + 16 * m, c4)) = b[m];
+          }
+        }
+        __syncthreads();
       }
-    }
+      for (int half = 0; half < (diag ? 1 : 2); ++half) {
+        // half 0: Rn[TI, TJ] rows i0 + r = A[r][c] - B[c][r]; half 1: Rn[TJ, TI] rows j0 + r = B[r][c] - A[c][r]
+        const float* Y = half == 0 ? sB : sA;
+        const int gr0 = half == 0 ? i0 : j0, gj0 = (half == 0 ? j0 : i0) + c4;
+        const int slot = 2 * (half == 0 ? tj : ti);
+        const int nv = FULL ? 4 : max(0, min(4, n - gj0));
+        const bool vs = FULL || (nv == 4 && (it.ldr % 4) == 0);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const int r = rr + 16 * m, gi = gr0 + r;
+          const float4 xv = half == 0 ? a[m] : b[m];
+          const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
+          float yv[4], v[4], rs = 0.f;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const bool ok = FULL || (gi < n && gj0 + k < n);
+            const float x = xs[k];
+            yv[k] = Y[sk_off(c4 + k, r)];
+            v[k] = ok ? x - yv[k] : 0.f;
+            rs += v[k] * v[k];
+            mx = fmaxf(mx, fabsf(v[k]));
+            dsum += v[k] * x;
+          }
+          if (FULL || (gi < n && nv > 0)) st4_split(it.r_hi, it.r_lo, (long long)gi * it.ldr + gj0, v, vs, nv);
+          if (r1 && (FULL || (gi < n && nv > 0)))  // q^T of the updated q: row gi is the transposed operand above
+            st4_split(it.qt_hi, it.qt_lo, (long long)gi * it.ldqt + gj0, yv, FULL || (nv == 4 && (it.ldqt % 4) == 0), nv);
+          rs += __shfl_xor_sync(0xffffffffu, rs, 1);
+          rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+          rs += __shfl_xor_sync(0xffffffffu, rs, 4);
+          rs += __shfl_xor_sync(0xffffffffu, rs, 8);
+          if ((t & 15) == 0 && (FULL || gi < n)) it.part_row[(long long)slot * n + gi] = rs;
+        }
+      }
+    };
+    if (full)
+      body(std::true_type());
+    else
+      body(std::false_type());
     mx = warp_max(mx);
     dsum = warp_sum(dsum);
     if (lane == 0) {
