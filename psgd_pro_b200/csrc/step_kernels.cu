@@ -76,6 +76,11 @@ PSGD_DEVI float normal1(unsigned long long s, uint32_t k0, uint32_t k1) {
 }
 
 // ---- gradient staging ------------------------------------------------------------------------------------------
+// floor(k / d) for 0 <= k < 8 d: for d <= 2^16 by one float multiply ((k + 1/2) / d lies at least 1 / (2 d) from
+// every integer, far more than the rounding error of (k + 1/2) * (1/d), below 2^-20 for quotients under 8; checked
+// exhaustively for every such d), else by integer division.
+PSGD_DEVI int div_small(int k, int d, float inv_d) { return d <= 65536 ? (int)(((float)k + 0.5f) * inv_d) : k / d; }
+
 // PREP_NORMAL rows r0 .. r0 + rows - 1 in 8-element vectors (16-byte bf16 G chunks, two for fp32 G; 16-byte
 // operand stores). Each thread first requests PREP_VEC vectors' G chunks into its own shared-memory slots
 // (cp.async: the loads are in flight together without holding registers), then converts them one at a time.
@@ -93,12 +98,13 @@ PSGD_DEVI void prep_rows_vec8(const PsgdPrepItem& it, long long r0, int rows, fl
                               uint32_t k1, uint4* stage) {
   constexpr int PV = BF16 ? PREP_VEC : PREP_VEC / 2, CH = BF16 ? 1 : 2;  // vectors per batch, chunks per vector
   const int nvr = it.n2 >> 3, nvec = rows * nvr, t = threadIdx.x;
+  const float inv_nvr = 1.f / (float)nvr;
   for (int base = t; base < nvec; base += blockDim.x * PV) {
 #pragma unroll
     for (int s = 0; s < PV; ++s) {
       const int j = base + s * blockDim.x;
       if (j < nvec) {
-        const int r = j / nvr;
+        const int r = div_small(j, nvr, inv_nvr);
         const long long idx = (r0 + r) * it.n2 + (long long)(j - r * nvr) * 8;
         const char* src = reinterpret_cast<const char*>(it.g) + idx * (BF16 ? 2 : 4);
 #pragma unroll
@@ -110,7 +116,7 @@ PSGD_DEVI void prep_rows_vec8(const PsgdPrepItem& it, long long r0, int rows, fl
     for (int s = 0; s < PV; ++s) {
       const int j = base + s * blockDim.x;
       if (j >= nvec) break;
-      const int r = j / nvr;
+      const int r = div_small(j, nvr, inv_nvr);
       const long long row = r0 + r, col = (long long)(j - r * nvr) * 8, idx = row * it.n2 + col;
       float x[8];
       if (BF16) {
@@ -742,7 +748,7 @@ PSGD_DEVI void unpack8(const uint4& u, float* f) {
 // LO: the operands carry lo halves (fp32 mode); without them that code is compiled out (fewer registers, more
 // blocks per SM).
 template <bool LO>
-__global__ void __launch_bounds__(256) rot_kernel(const PsgdRotItem* __restrict__ items,
+__global__ void __launch_bounds__(256, LO ? 2 : 3) rot_kernel(const PsgdRotItem* __restrict__ items,
                                                  const uint32_t* __restrict__ work, int nwork) {
   for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
     const PsgdRotItem& it = items[work[2 * w]];
@@ -750,6 +756,7 @@ __global__ void __launch_bounds__(256) rot_kernel(const PsgdRotItem* __restrict_
     const float a = *it.alpha, inv_s = *it.beta, half_a2 = 0.5f * a * a;
     const int nvec = (int)(it.ldr / 8);
     const int total = min(ROT_ROWS, it.n - r0) * nvec;
+    const float inv_nvec = 1.f / (float)nvec;
     __nv_bfloat16* rbase_h = reinterpret_cast<__nv_bfloat16*>(it.r_hi);
     __nv_bfloat16* rbase_l = LO ? reinterpret_cast<__nv_bfloat16*>(it.r_lo) : nullptr;
     const __nv_bfloat16* sbase_h = reinterpret_cast<const __nv_bfloat16*>(it.s_hi);
@@ -760,7 +767,8 @@ __global__ void __launch_bounds__(256) rot_kernel(const PsgdRotItem* __restrict_
 #pragma unroll
       for (int u = 0; u < ROT_VEC; ++u) {
         const int k = k0 + u * blockDim.x;
-        const long long row = r0 + k / nvec, col = (long long)(k % nvec) * 8;
+        const int rloc = div_small(k, nvec, inv_nvec);
+        const long long row = r0 + rloc, col = (long long)(k - rloc * nvec) * 8;
         ro[u] = row * it.ldr + col;
         so[u] = row * it.lds + col;
         if (k < total) {
