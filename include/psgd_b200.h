@@ -232,6 +232,22 @@ typedef struct PsgdRotItem {
 int psgd_rot(const PsgdRotItem* items, const uint32_t* work, int nwork, int has_lo, int* dev_err,
              cudaStream_t stream);
 
+/* Trace of the Procrustes line search, sum_ij S_ij Q_ij with S = Rn Rn^T (psgd_pro_fast.py:149-151): S as stored
+ * (bf16 hi, plus lo when s_lo != NULL; leading dimension lds) against the fp32 n x n Q, both read row-major once.
+ * Work entries: (item, first row of a block of PSGD_TRACE_ROWS rows); entry (item, r0) writes the block's sum to
+ * part[r0 / PSGD_TRACE_ROWS] (a fixed-order block reduction), so sum(part[0 .. ceil(n / PSGD_TRACE_ROWS))) is the
+ * trace. A separate pass because the alternative, the S product's epilogue reading Q at each tile and at its mirror,
+ * cost more than this pass's 6 bytes per element. */
+#define PSGD_TRACE_ROWS 8
+typedef struct PsgdTraceItem {
+  const float* q; int n;
+  const void* s_hi; const void* s_lo; long long lds;
+  float* part;
+} PsgdTraceItem;
+/* has_lo: the items' s_lo are set (fp32 mode; with 0 they are ignored). */
+int psgd_trace(const PsgdTraceItem* items, const uint32_t* work, int nwork, int has_lo, int* dev_err,
+               cudaStream_t stream);
+
 /* Clip and apply (psgd_pro.py:371-381, branch-free as psgd_pro_fast.py:426-438): per parameter
  * avg = sqrt(sum(part) / numel), g = clamp(pg * min(1, max_avg / avg), +-max_elem), param -= lr_params * g.
  * Work items are (item, chunk) pairs over chunks of PSGD_APPLY_CHUNK elements. */

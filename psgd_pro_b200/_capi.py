@@ -69,6 +69,10 @@ class RotItem(ctypes.Structure):
                 ("lds", c_ll), ("alpha", c_vp), ("beta", c_vp)]
 
 
+class TraceItem(ctypes.Structure):
+    _fields_ = [("q", c_vp), ("n", c_int), ("s_hi", c_vp), ("s_lo", c_vp), ("lds", c_ll), ("part", c_vp)]
+
+
 class ApplyItem(ctypes.Structure):
     _fields_ = [("param", c_vp), ("param_bf16", c_int), ("numel", c_ll), ("pg", c_vp), ("part", c_vp),
                 ("nparts", c_int), ("scale", c_vp)]
@@ -87,6 +91,7 @@ class BalanceParam(ctypes.Structure):
 PSGD_PREP_NORMAL, PSGD_PREP_TRANS, PSGD_PREP_DIRECT = 0, 1, 2
 PREP_ROWS = 8
 ROT_ROWS = 8
+TRACE_ROWS = 8
 SKEW_TILE = 64
 FAC_SCRATCH = 32   # floats of scratch per diagonal factor item
 PSGD_FACTOR_DENSE, PSGD_FACTOR_RANK1, PSGD_FACTOR_DIAG, PSGD_FACTOR_SKEW = 0, 1, 2, 3
@@ -109,6 +114,7 @@ SIGNATURES = [
     ("psgd_skew", c_int, [c_vp, c_vp, c_int, c_vp, c_vp]),
     ("psgd_skew_rank1", c_int, [c_vp, c_vp, c_int, c_vp, c_vp]),
     ("psgd_rot", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp]),
+    ("psgd_trace", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp]),
     ("psgd_apply", c_int, [c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_vp]),
     ("psgd_balance", c_int, [c_vp, c_vp, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_vp]),
     ("psgd_apply_noalloc", c_int, [c_vp, c_int, c_vp, c_ll, c_float, c_float, c_float, c_vp]),

@@ -806,6 +806,83 @@ __global__ void __launch_bounds__(256, LO ? 2 : 3) rot_kernel(const PsgdRotItem*
   }
 }
 
+// ---- trace of S o Q ----------------------------------------------------------------------------------------------
+// Work entries (item, first row of TRACE_ROWS rows). 8-element vectors of S (16-byte bf16 loads) and Q (two 16-byte
+// loads), TRACE_VEC vectors per thread requested before the first use; rows whose Q vectors are not 16-byte aligned
+// (n % 4 != 0) and the tail columns of n % 8 != 0 go element by element.
+constexpr int TRACE_ROWS = PSGD_TRACE_ROWS;
+constexpr int TRACE_VEC = 4;
+
+// LO: the items carry lo halves of S (fp32 mode); without them that code is compiled out (fewer registers, more
+// blocks per SM).
+template <bool LO>
+__global__ void __launch_bounds__(256, LO ? 2 : 3) trace_kernel(const PsgdTraceItem* __restrict__ items,
+                                                               const uint32_t* __restrict__ work, int nwork) {
+  __shared__ float red[8];
+  for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
+    const PsgdTraceItem& it = items[work[2 * w]];
+    const int r0 = (int)work[2 * w + 1], n = it.n;
+    const int rows = min(TRACE_ROWS, n - r0);
+    const __nv_bfloat16* sh = reinterpret_cast<const __nv_bfloat16*>(it.s_hi);
+    const __nv_bfloat16* sl = LO ? reinterpret_cast<const __nv_bfloat16*>(it.s_lo) : nullptr;
+    const bool vec = (n % 4) == 0 && (reinterpret_cast<uintptr_t>(it.q) & 15) == 0 && (it.lds % 8) == 0 &&
+                     (reinterpret_cast<uintptr_t>(sh) & 15) == 0 && (reinterpret_cast<uintptr_t>(sl) & 15) == 0;
+    const int nv = vec ? n / 8 : 0, total = rows * nv;
+    const float inv_nv = nv > 0 ? 1.f / (float)nv : 0.f;
+    float acc = 0.f;
+    for (int k0 = threadIdx.x; k0 < total; k0 += TRACE_VEC * blockDim.x) {
+      uint4 hv[TRACE_VEC], lv[LO ? TRACE_VEC : 1];
+      float4 qa[TRACE_VEC], qb[TRACE_VEC];
+#pragma unroll
+      for (int u = 0; u < TRACE_VEC; ++u) {
+        const int k = k0 + u * blockDim.x;
+        if (k < total) {
+          const int rl = div_small(k, nv, inv_nv);
+          const long long row = r0 + rl, col = (long long)(k - rl * nv) * 8;
+          hv[u] = *reinterpret_cast<const uint4*>(sh + row * it.lds + col);
+          if (LO && sl) lv[LO ? u : 0] = *reinterpret_cast<const uint4*>(sl + row * it.lds + col);
+          const float4* qp = reinterpret_cast<const float4*>(it.q + row * n + col);
+          qa[u] = qp[0];
+          qb[u] = qp[1];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < TRACE_VEC; ++u) {
+        if (k0 + u * blockDim.x >= total) continue;
+        float sv[8];
+        unpack8(hv[u], sv);
+        if (LO && sl) {
+          float l[8];
+          unpack8(lv[LO ? u : 0], l);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) sv[i] += l[i];
+        }
+        const float qv[8] = {qa[u].x, qa[u].y, qa[u].z, qa[u].w, qb[u].x, qb[u].y, qb[u].z, qb[u].w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc = fmaf(sv[i], qv[i], acc);
+      }
+    }
+    // elements not covered by whole vectors: every column of a row (vec false) or the n % 8 tail
+    const int c0 = nv * 8, ntail = n - c0;
+    for (int k = threadIdx.x; k < rows * ntail; k += blockDim.x) {
+      const int rl = k / ntail;
+      const long long row = r0 + rl, col = c0 + (k - rl * ntail);
+      float sv = __bfloat162float(sh[row * it.lds + col]);
+      if (LO && sl) sv += __bfloat162float(sl[row * it.lds + col]);
+      acc = fmaf(sv, it.q[row * n + col], acc);
+    }
+    acc = warp_sum(acc);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.f;
+      for (int k = 0; k < (int)(blockDim.x >> 5); ++k) t += red[k];
+      it.part[r0 / TRACE_ROWS] = t;
+    }
+    __syncthreads();
+  }
+}
+
 // ---- clip + apply ------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) clip_scale_kernel(const PsgdApplyItem* __restrict__ items,
                                                         const float* __restrict__ hyper) {
@@ -1043,6 +1120,15 @@ extern "C" int psgd_rot(const PsgdRotItem* items, const uint32_t* work, int nwor
   if (nwork == 0) return PSGD_OK;
   if (has_lo) rot_kernel<true><<<grid_for(rot_kernel<true>, 256, nwork), 256, 0, stream>>>(items, work, nwork);
   else rot_kernel<false><<<grid_for(rot_kernel<false>, 256, nwork), 256, 0, stream>>>(items, work, nwork);
+  return launched();
+}
+
+extern "C" int psgd_trace(const PsgdTraceItem* items, const uint32_t* work, int nwork, int has_lo, int* dev_err,
+                          cudaStream_t stream) {
+  if (!items || !work || nwork < 0) return PSGD_EINVAL;
+  if (nwork == 0) return PSGD_OK;
+  if (has_lo) trace_kernel<true><<<grid_for(trace_kernel<true>, 256, nwork), 256, 0, stream>>>(items, work, nwork);
+  else trace_kernel<false><<<grid_for(trace_kernel<false>, 256, nwork), 256, 0, stream>>>(items, work, nwork);
   return launched();
 }
 

@@ -103,7 +103,7 @@ class _Factor:
             self.r_rows = torch.zeros(self.T32, n, device=dev)
             self.r_max = torch.zeros(self.T32 * self.T32, device=dev)
             self.r_dot = torch.zeros(self.T32 * self.T32, device=dev)
-            self.s_dot = torch.zeros(self.Tn * cdiv(n, self.sbn), device=dev)
+            self.s_dot = torch.zeros(cdiv(n, _capi.TRACE_ROWS), device=dev)  # trace partials of S o Q
             self.refresh_operands()
         elif kind == "diag":
             self.q = torch.full((n,), float(scale), device=dev)
@@ -361,7 +361,7 @@ class _Plan:
         self.nlb_skh_dev, self.nlb_skh_n = self._nlb_prep(dense, skew=True)
         self.g_skh = self._nlb_chain(dense, skew=True)
         # U17: S = Rn Rn^T with sum(S .* Q) partials
-        self.g_u17 = self.group([self.syrk(f.R, f.n, f.n, out_hi=f.T[0], out_lo=f.T[1], dot_aux=f.q, part_dot=f.s_dot)
+        self.g_u17 = self.group([self.syrk(f.R, f.n, f.n, out_hi=f.T[0], out_lo=f.T[1])
                                  for f in dense])
         # U18: Procrustes step size
         si = []
@@ -374,6 +374,16 @@ class _Plan:
             it.alpha, it.beta = self.s(f, S_AM).data_ptr(), self.s(f, S_BM).data_ptr()
             si.append(it)
         self.skf_dev, self.skf_n = _upload(_capi.FactorItem, si, dev), len(si)
+        # sum S o Q for the step size: one row-major pass over the stored S and Q
+        ti, tw = [], []
+        for f in dense:
+            it = _capi.TraceItem()
+            it.q, it.n, it.part = f.q.data_ptr(), f.n, f.s_dot.data_ptr()
+            it.s_hi, it.s_lo, it.lds = K.ptr(f.T[0]), K.ptr(f.T[1]), f.T[0].stride(0)
+            ti.append(it)
+            tw += [(len(ti) - 1, r0) for r0 in range(0, f.n, _capi.TRACE_ROWS)]
+        self.trace_dev = _upload(_capi.TraceItem, ti, dev)
+        self.trace_work, self.trace_n = _work(tw, dev)
         # U19: M = a/s Rn + a^2/(2 s^2) S (in place of Rn)
         ri, rw = [], []
         for f in dense:
@@ -552,6 +562,9 @@ class _Plan:
             tr(f"nlb_skh{k}")
         self._launch(self.g_u17)
         tr("S")
+        check(L.psgd_trace(self.trace_dev.data_ptr(), self.trace_work.data_ptr(), self.trace_n, int(self.split == 3),
+                           err, st), "trace")
+        tr("trace")
         check(L.psgd_factor_update(self.skf_dev.data_ptr(), self.skf_n, hy, err, st), "procrustes scalars")
         tr("procrustes_scalars")
         check(L.psgd_rot(self.rot_dev.data_ptr(), self.rot_work.data_ptr(), self.rot_n, int(self.split == 3), err, st),
@@ -594,6 +607,7 @@ class _Plan:
             n += int(self.nlb_spd_n > 0) + int(self.nlb_skh_n > 0)  # norm-bound starts
             n += 2 * int(self.fac_n > 0) + 2 * int(self.skf_n > 0)  # factor scalars: two launches each
             n += int(self.skew_n > 0) + int(self.skew1_n > 0) + int(self.rot_n > 0)  # skew (two kinds), rot
+            n += int(self.trace_n > 0)  # trace of S o Q
             groups += [self.g_u1, self.g_u2, self.g_u3, self.g_u3r, self.g_u10, self.g_u17, self.g_u20, self.g_u22]
             groups += self.g_spd + self.g_skh
         return n + sum(g is not None for g in groups)

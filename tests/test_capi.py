@@ -42,5 +42,6 @@ def test_header_constants_match_binding():
     assert int(defs["PSGD_PREP_ROWS"]) == _capi.PREP_ROWS
     assert int(defs["PSGD_ROT_ROWS"]) == _capi.ROT_ROWS
     assert int(defs["PSGD_SKEW_TILE"]) == _capi.SKEW_TILE
+    assert int(defs["PSGD_TRACE_ROWS"]) == _capi.TRACE_ROWS
     assert int(defs["PSGD_FAC_SCRATCH"]) == _capi.FAC_SCRATCH
     assert int(defs["PSGD_APPLY_CHUNK"]) == _capi.APPLY_CHUNK
