@@ -308,8 +308,10 @@ def main():
     # computes, and step i's metric is read once the step has finished; all of it inside the timed region.
     e2e = None
     ek = args.e2e_steps or max(2, min(args.steps, 5))
-    host = [[g.cpu().pin_memory() for g in grads[0]], [g.cpu().pin_memory() for g in grads[1]]]
-    bufs = [grads[0], grads[1]]
+    # each rank copies in the gradients of the parameters it owns: the sharded step reads only those (at N = 1, all)
+    own = list(opt.owned)
+    host = [[grads[j][i].cpu().pin_memory() for i in own] for j in range(2)]
+    bufs = [[grads[j][i] for i in own] for j in range(2)]
     nown = len(inner._plan.params) if inner is not None else 0
     mets = [torch.empty(max(1, nown), dtype=torch.float32).pin_memory() for _ in range(2)]
     main, copy_stream = torch.cuda.current_stream(), torch.cuda.Stream()
@@ -337,7 +339,7 @@ def main():
         if i + 1 < ek:
             h2d(i + 1)
         main.wait_event(copied[b])
-        opt.step_math(bufs[b])
+        opt.step_math(grads[b])  # bufs[b] holds grads[b]'s owned tensors, just refilled
         if inner is not None:
             mets[b].copy_(inner._plan.clip[:max(1, nown)], non_blocking=True)
         met_ready[b].record(main)
@@ -355,6 +357,10 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e_ms = float(t.item())
     h2d = sum(g.numel() * g.element_size() for g in host[0])
+    if world > 1:  # whole job: every rank's copies
+        t = torch.tensor([float(h2d)], device=dev, dtype=torch.float64)
+        dist.all_reduce(t)
+        h2d = int(t.item())
     e2e = {"value": 1000.0 / e_ms, "unit": "steps/s", "h2d_bytes_per_step": h2d,
            "d2h_bytes_per_step": mets[0].numel() * 4, "overlap": "next step's H2D copy during this step"}
 
