@@ -1,7 +1,7 @@
 """Generates the golden vectors in tests/golden/*.npz by running the reference implementation itself.
 
 Run here, where the reference checkout exists (it does not travel to GPU boxes):
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/reference      (or PSGD_REFERENCE=/path/to/reference)
 The reference imports the third-party opt_einsum, which is absent; tests/golden/standin provides the three names
 it uses (see that package's docstring). Every Gaussian and uniform draw the reference makes through torch
 (randn_like(G) for the damping noise, randn(32, n) for the norm-bound starts, rand([]) for the update and
@@ -19,7 +19,7 @@ import types
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("PSGD_REFERENCE", "")
 
 SCENARIOS = [
     # config 1 of the benchmark plan: one fp32 256 x 512 weight, both factors dense, 10 steps
@@ -212,6 +212,8 @@ def run_units(torch, psgd_pro, fast):
 
 
 def main():
+    if not REF or not os.path.isdir(REF):
+        sys.exit("usage: make_golden.py /path/to/reference (the psgd_pro checkout; or set PSGD_REFERENCE)")
     sys.path.insert(0, os.path.join(HERE, "standin"))
     sys.path.insert(0, REF)
     import torch
