@@ -52,16 +52,23 @@ extern "C" {
  *     are never touched, so the buffer must start at zero once and the sum over all slots is the row sum;
  *   diag_out[r] = value(r, r); part_dot[tm * tiles_n + tn] = the tile's share of sum(S .* dot_aux) over both
  *     triangles (again zero-initialised once; the total is the sum of all entries).
+ *   out_packed (SYRK only): the upper triangle as n(n+1)/2 fp32 values, row-major packed, (r, c >= r) at
+ *     r n - r (r - 1) / 2 + c - r (the PACKED store of kernels/k2.py:78-80); may be the only output.
+ * mode PSGD_GEMM_TRMM: A is upper triangular (A[r, k] = 0 for k < r; the caller stages it with zeros there) and
+ *   M == K: tile (tm, tn) reduces over k >= its first row only, so the zero blocks left of the diagonal are neither
+ *   loaded nor multiplied (n^2 (n + 1) useful FLOPs for a square T X instead of 2 n^3). No counterpart in the
+ *   reference (the triangular-times-dense product of its benchmark plan).
  */
 #define PSGD_GEMM_PLAIN 0
 #define PSGD_GEMM_SYRK 1
+#define PSGD_GEMM_TRMM 2
 
 typedef struct PsgdGemmSpec {
   const void* a_hi; const void* a_lo; long long lda;   /* A: M x K bf16 */
   const void* b_hi; const void* b_lo; long long ldb;   /* B: N x K bf16 */
   int M, N, K;
   int bn;       /* tile width: 16, 32, 64, 128 or 256 (<= 128 with split = 3) */
-  int mode;     /* PSGD_GEMM_PLAIN or PSGD_GEMM_SYRK */
+  int mode;     /* PSGD_GEMM_PLAIN, PSGD_GEMM_SYRK or PSGD_GEMM_TRMM */
   float alpha, beta;
   const float* alpha_ptr; const float* beta_ptr;
   const float* aux; long long ld_aux;
@@ -72,6 +79,7 @@ typedef struct PsgdGemmSpec {
   float* part_tile; float* part_col; float* part_row; float* diag_out;
   const float* dot_aux; long long ld_dot; float* part_dot;
   const float* cs_part; int cs_T; int cs_mode; const float* cs_nf;
+  float* out_packed;
 } PsgdGemmSpec;
 
 /* One problem, launched directly (its descriptor travels as a kernel parameter). Replaces the per-call cuBLAS
@@ -279,6 +287,41 @@ int psgd_balance(const PsgdBalanceFactor* factors, const PsgdBalanceParam* param
                  const uint32_t* work_max, int nwork_max, const uint32_t* work_apply, int nwork_apply, int* dev_err,
                  cudaStream_t stream);
 
+/* ---------------------------------------------------------------------------------------------------------
+ * Symmetric matrices in storage form (kernels/ops.py:7-11): PSGD_SYM_SQUARE, an n x n fp32 square (leading
+ * dimension lda) whose upper triangle (j >= i) holds the matrix, the lower triangle never read (it may hold
+ * anything, NaN included, kernels/ops.py:9); PSGD_SYM_PACKED, the row-major packed upper triangle, n(n+1)/2 fp32
+ * values with (i, j >= i) at i n - i (i - 1) / 2 + j - i (kernels/k2.py:78-80). The full matrix is
+ * A(i, j) = U(i, j) for j >= i and sign * U(j, i) below: sign 1 symmetric, -1 skew-symmetric (diagonal taken as
+ * zero, as kernels/k1.cu:41-50 does), 0 upper triangular (zeros below; the staging of a TRMM operand).
+ * psgd_sym_expand reads only the stored triangle, once, in pairs of PSGD_SYM_TILE-square tiles (work entries
+ * (item, (I << 16) | J), I <= J), and writes each optional output:
+ *   out_hi / out_lo (bf16 hi/lo, leading dimension ld_out): the full matrix as a tensor-core operand;
+ *   out_f32 (ld_f32): the full matrix in fp32 (kernels/k2.py:88-103 unpack);
+ *   part_row[slot * n + i]: sums of squares of row i over the columns of 64-column block slot (every slot written);
+ *   part_max[I * T + J] (T = ceil(n / 64)): max |A| over the pair's tiles;  diag[i] = A(i, i).
+ * psgd_sym_reduce finishes tri_rownorm2 (kernels/k1.cu:296-307): row_sq[i] = sum of part_row over the slots,
+ * *absmax = max of part_max (max_n: the largest n of the items). */
+#define PSGD_SYM_TILE 64
+#define PSGD_SYM_SQUARE 0
+#define PSGD_SYM_PACKED 1
+typedef struct PsgdSymItem {
+  const float* a; long long lda; int form; int n; int sign;
+  void* out_hi; void* out_lo; long long ld_out;
+  float* out_f32; long long ld_f32;
+  float* part_row; float* part_max; float* diag;
+  float* row_sq; float* absmax;
+} PsgdSymItem;
+int psgd_sym_expand(const PsgdSymItem* items, const uint32_t* work, int nwork, int* dev_err, cudaStream_t stream);
+int psgd_sym_reduce(const PsgdSymItem* items, int nitems, int max_n, int* dev_err, cudaStream_t stream);
+
+/* End of a norm lower bound (psgd_pro.py:40-41, psgd_pro_fast.py:43): *out = *nf * max_c sqrt(sum_t part[t * ncols
+ * + c]) over the column sums of squares of the last subspace product, one block per item. */
+typedef struct PsgdNlbFinishItem {
+  const float* nf; const float* part; int slots; int ncols; float* out;
+} PsgdNlbFinishItem;
+int psgd_nlb_finish(const PsgdNlbFinishItem* items, int nitems, int* dev_err, cudaStream_t stream);
+
 /* Clip and apply for one parameter without any device memory from the caller. It has no counterpart in the
  * reference, which always works through torch and so always allocates. It exists for callers that cannot
  * allocate device memory: a plugin whose host application owns every device allocation, code that runs inside
@@ -293,7 +336,9 @@ int psgd_balance(const PsgdBalanceFactor* factors, const PsgdBalanceParam* param
  * The first call on a device looks up the array's device address with that device current; make that first call
  * before any stream capture. All calls on a device share the array and leave their sums in it; each call writes
  * every slot it reads before reading it, so nothing carries over, but calls whose kernels overlap on the GPU (on
- * different streams) race on the array and produce wrong results. */
+ * different streams) race on the array and produce wrong results. When a CUDA error from earlier work is already
+ * pending on the calling thread, the call launches nothing and returns PSGD_ELAUNCH, leaving that error in place.
+ * Non-finite values propagate as in the reference: a NaN in pg reaches the parameter. */
 #define PSGD_APPLY_NOALLOC_SLOTS 4096
 #define PSGD_APPLY_NOALLOC_MAX_NUMEL (4096LL * PSGD_APPLY_CHUNK)
 int psgd_apply_noalloc(void* param, int param_bf16, const float* pg, long long numel, float lr_params,

@@ -15,7 +15,7 @@ ERRORS = {-1: "invalid argument (shape, stride, alignment or mode)", -2: "CUDA l
           -3: "TMA descriptor encoding failed", -4: "caller table or workspace too small",
           -5: "size beyond the fixed scratch of the no-allocation entry point"}
 
-PSGD_GEMM_PLAIN, PSGD_GEMM_SYRK = 0, 1
+PSGD_GEMM_PLAIN, PSGD_GEMM_SYRK, PSGD_GEMM_TRMM = 0, 1, 2
 
 
 class GemmSpec(ctypes.Structure):
@@ -35,6 +35,7 @@ class GemmSpec(ctypes.Structure):
         ("part_tile", c_vp), ("part_col", c_vp), ("part_row", c_vp), ("diag_out", c_vp),
         ("dot_aux", c_vp), ("ld_dot", c_ll), ("part_dot", c_vp),
         ("cs_part", c_vp), ("cs_T", c_int), ("cs_mode", c_int), ("cs_nf", c_vp),
+        ("out_packed", c_vp),
     ]
 
 
@@ -88,6 +89,16 @@ class BalanceParam(ctypes.Structure):
     _fields_ = [("f0", c_int), ("nf", c_int)]
 
 
+class SymItem(ctypes.Structure):
+    _fields_ = [("a", c_vp), ("lda", c_ll), ("form", c_int), ("n", c_int), ("sign", c_int),
+                ("out_hi", c_vp), ("out_lo", c_vp), ("ld_out", c_ll), ("out_f32", c_vp), ("ld_f32", c_ll),
+                ("part_row", c_vp), ("part_max", c_vp), ("diag", c_vp), ("row_sq", c_vp), ("absmax", c_vp)]
+
+
+class NlbFinishItem(ctypes.Structure):
+    _fields_ = [("nf", c_vp), ("part", c_vp), ("slots", c_int), ("ncols", c_int), ("out", c_vp)]
+
+
 PSGD_PREP_NORMAL, PSGD_PREP_TRANS, PSGD_PREP_DIRECT = 0, 1, 2
 PREP_ROWS = 8
 ROT_ROWS = 8
@@ -98,6 +109,8 @@ PSGD_FACTOR_DENSE, PSGD_FACTOR_RANK1, PSGD_FACTOR_DIAG, PSGD_FACTOR_SKEW = 0, 1,
 HY_LR_PRECOND, HY_BETA_L, HY_DAMPING, HY_LR_PARAMS, HY_MAX_AVG, HY_MAX_ELEM, HY_MOM_BETA = range(7)
 HY_NOISE, HY_NOISE_KEY0, HY_NOISE_KEY1, HY_COUNT = 7, 8, 9, 12
 APPLY_CHUNK = 8192
+SYM_TILE = 64
+PSGD_SYM_SQUARE, PSGD_SYM_PACKED = 0, 1
 
 # (name, restype, argtypes) of every exported entry point; tests check that each symbol is present.
 SIGNATURES = [
@@ -118,6 +131,9 @@ SIGNATURES = [
     ("psgd_apply", c_int, [c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_vp]),
     ("psgd_balance", c_int, [c_vp, c_vp, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_vp]),
     ("psgd_apply_noalloc", c_int, [c_vp, c_int, c_vp, c_ll, c_float, c_float, c_float, c_vp]),
+    ("psgd_sym_expand", c_int, [c_vp, c_vp, c_int, c_vp, c_vp]),
+    ("psgd_sym_reduce", c_int, [c_vp, c_int, c_int, c_vp, c_vp]),
+    ("psgd_nlb_finish", c_int, [c_vp, c_int, c_vp, c_vp]),
 ]
 
 _lib = None

@@ -7,6 +7,8 @@
 
 #include <float.h>
 
+#include <atomic>
+
 namespace psgd {
 namespace {
 
@@ -57,11 +59,13 @@ __global__ void __launch_bounds__(NA_THREADS) na_apply_kernel(void* param, int p
   for (int t = threadIdx.x; t < nslots; t += NA_THREADS) s += scratch[t];
   const float total = na_block_sum(s, red);
   const float avg = sqrtf(total / (float)numel);
-  const float sc = fminf(max_avg / avg, 1.f);
+  // as psgd_pro.py:374-376: scale only when avg > max_avg (a NaN avg leaves the scale 1)
+  const float sc = avg > max_avg ? max_avg / avg : 1.f;
   const long long base = (long long)blockIdx.x * NA_CHUNK;
   const long long end = min(base + (long long)NA_CHUNK, numel);
   for (long long k = base + threadIdx.x; k < end; k += NA_THREADS) {
-    const float g = fminf(fmaxf(pg[k] * sc, -max_elem), max_elem);
+    const float x = pg[k] * sc;
+    const float g = isnan(x) ? x : fminf(fmaxf(x, -max_elem), max_elem);  // torch.clamp keeps NaN
     if (param_bf16) {
       __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(param);
       p[k] = __float2bfloat16_rn(__bfloat162float(p[k]) - lr * g);
@@ -74,16 +78,20 @@ __global__ void __launch_bounds__(NA_THREADS) na_apply_kernel(void* param, int p
 
 // Device address of g_apply_scratch on the current device, looked up once per device with that device current.
 // In host code the name g_apply_scratch is only a host-side stand-in, never a device address.
+// The cache is shared by host threads: each entry is atomic (threads that race on the first call of a device
+// look the address up twice and store the same value).
 float* scratch_on_current_device() {
-  static float* addr[64] = {};
+  static std::atomic<float*> addr[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (addr[dev] == nullptr) {
+  float* a = addr[dev].load(std::memory_order_acquire);
+  if (a == nullptr) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_apply_scratch) != cudaSuccess || p == nullptr) return nullptr;
-    addr[dev] = static_cast<float*>(p);
+    a = static_cast<float*>(p);
+    addr[dev].store(a, std::memory_order_release);
   }
-  return addr[dev];
+  return a;
 }
 
 }  // namespace
@@ -95,6 +103,9 @@ extern "C" int psgd_apply_noalloc(void* param, int param_bf16, const float* pg, 
   if (param == nullptr || pg == nullptr || numel < 0) return PSGD_EINVAL;
   if (numel > PSGD_APPLY_NOALLOC_MAX_NUMEL) return PSGD_ELIMIT;
   if (numel == 0) return PSGD_OK;
+  // An error left pending by earlier, unrelated work is not this call's: launch nothing and leave it in place
+  // for its owner to read (the launch checks below would otherwise report and clear it).
+  if (cudaPeekAtLastError() != cudaSuccess) return PSGD_ELAUNCH;
   float* scratch = scratch_on_current_device();
   if (scratch == nullptr) return PSGD_ELAUNCH;
   const int nslots = (int)((numel + NA_CHUNK - 1) / NA_CHUNK);

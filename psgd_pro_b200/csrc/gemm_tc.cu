@@ -85,6 +85,9 @@ PSGD_DEVI void st4f(float* p, const float* x, int n, bool vec) {
   }
 }
 
+// Row-major packed upper triangle of an n x n matrix: (r, c >= r) at r n - r (r - 1) / 2 + c - r.
+PSGD_DEVI long long packed_off(long long r, long long c, long long n) { return r * n - (r * (r - 1)) / 2 + (c - r); }
+
 PSGD_DEVI uint32_t pack_bf16x2(__nv_bfloat16 a, __nv_bfloat16 b) {
   return (uint32_t)__bfloat16_as_ushort(a) | ((uint32_t)__bfloat16_as_ushort(b) << 16);
 }
@@ -146,6 +149,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmDesc& d, int tm, int tn,
   const float s_alpha = sd.alpha, s_beta = sd.beta;
   const float* s_alpha_ptr = sd.alpha_ptr;
   const float* s_beta_ptr = sd.beta_ptr;
+  float* __restrict__ s_out_packed = sd.out_packed;
   const int d_tiles_n = d.tiles_n;
 
   const int bn = s_bn;
@@ -311,6 +315,12 @@ __device__ __forceinline__ void epilogue_tile(const GemmDesc& d, int tm, int tn,
               for (int i = 0; i < 4; ++i)
                 if (i >= first && i < ncv) dsum += x[i] * dd[i];
             }
+            if (s_out_packed) {
+              const long long pb = packed_off(gr, gcb, s_N);
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                if (i >= first && i < ncv) s_out_packed[pb + i] = x[i];
+            }
           }
         }
       }
@@ -461,6 +471,7 @@ __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn,
   const long long s_ld_dot = sd.ld_dot;
   float* __restrict__ s_part_dot = sd.part_dot;
   float* __restrict__ s_diag_out = sd.diag_out;
+  float* __restrict__ s_out_packed = sd.out_packed;
   const int d_tiles_n = d.tiles_n;
   const long long m0 = (long long)tm * BM, n0 = (long long)tn * bn;
   const long long row0 = m0 + q * 32;
@@ -580,6 +591,13 @@ __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn,
           *reinterpret_cast<float4*>(s_out_f32 + row * s_ld_f32 + colb) = make_float4(x[0], x[1], x[2], x[3]);
         if (out_hi) st4b(out_hi + row * s_ld_b + colb, out_lo ? out_lo + row * s_ld_b + colb : nullptr, x, 4, true);
         if (s_dot) dsum += x[0] * pv[it].x + x[1] * pv[it].y + x[2] * pv[it].z + x[3] * pv[it].w;
+        if (s_out_packed) {  // four consecutive values of row `row` (no vector store: the offsets are unaligned)
+          float* pp = s_out_packed + packed_off(row, colb, s_N);
+          pp[0] = x[0];
+          pp[1] = x[1];
+          pp[2] = x[2];
+          pp[3] = x[3];
+        }
       } else {  // EPI_SYRK on the diagonal: element i is direct when colb + i >= row, mirrored when >
         const int first = (int)max(-1LL, min(4LL, row - colb));
         const float dd[4] = {pv[it].x, pv[it].y, pv[it].z, pv[it].w};
@@ -593,6 +611,7 @@ __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn,
           csq[i] += (i > first) ? x2 : 0.f;
           if (i == first && s_diag_out) s_diag_out[row] = x[i];
           if (direct) {
+            if (s_out_packed) s_out_packed[packed_off(row, colb + i, s_N)] = x[i];
             if (s_out_f32) s_out_f32[row * s_ld_f32 + colb + i] = x[i];
             if (out_hi) {
               __nv_bfloat16 h, l;
@@ -723,6 +742,12 @@ __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn,
   named_sync(1, 128);
 }
 
+// First K block a tile reduces over: 0, or in TRMM mode (A upper triangular, M == K) the block holding the tile's
+// first row, m0 / kblock (the blocks before it multiply zeros). m0 < M = K, so every tile has at least one block.
+PSGD_HD int first_kblock(const PsgdGemmSpec& s, long long m0, int kblock) {
+  return s.mode == PSGD_GEMM_TRMM ? (int)(m0 / kblock) : 0;
+}
+
 // Grouped tile lists start with a header of uint32 values: the number of segments S (one per CTA), then S + 1
 // offsets; segment b holds the tiles of CTA b, entries [off_b, off_(b+1)) of the (problem, tm << 16 | tn) pairs
 // that follow the header.
@@ -819,8 +844,9 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
         get_tile(descs, tiles, t, p, tm, tn);
         const GemmDesc& d = descs[p];
         const int nk = (d.s.K + BK * C::KSUB - 1) / (BK * C::KSUB);
+        const int kb0 = first_kblock(d.s, tm * BM, BK * C::KSUB);
         const uint32_t sub_bytes = C::NOPS * (C::A_BYTES + d.s.bn * BK * 2);
-        for (int kb = 0; kb < nk; ++kb, ++g) {
+        for (int kb = kb0; kb < nk; ++kb, ++g) {
           const int s = g % STAGES;
           const uint32_t ph = (g / STAGES) & 1;
           // 64-deep blocks of this stage that hold any of K (no copy is issued past the end)
@@ -859,6 +885,7 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
         get_tile(descs, tiles, t, p, tm, tn);
         const GemmDesc& d = descs[p];
         const int nk = (d.s.K + BK * C::KSUB - 1) / (BK * C::KSUB);
+        const int kb0 = first_kblock(d.s, tm * BM, BK * C::KSUB);
         const int bn = d.s.bn;
         const uint32_t acc = i & 1, aph = (i >> 1) & 1;
         if (!mbar_wait(&tempty[acc], aph ^ 1, abort)) break;
@@ -866,7 +893,7 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
         const uint32_t dt = tmem_base + acc * BNMAX;
         const uint32_t idesc = idesc_bf16_m128(bn);
         bool ok = true;
-        for (int kb = 0; kb < nk; ++kb, ++g) {
+        for (int kb = kb0; kb < nk; ++kb, ++g) {
           const int s = g % STAGES;
           const uint32_t ph = (g / STAGES) & 1;
           if (!mbar_wait(&full[s], ph, abort)) {
@@ -881,7 +908,7 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
 #pragma unroll
             for (int kk = 0; kk < BK / 16; ++kk) {
               const uint64_t ad = sdesc_k_sw128(a_hi + kk * 32), bd = sdesc_k_sw128(b_hi + kk * 32);
-              umma_bf16(dt, ad, bd, idesc, (kb | j | kk) != 0);
+              umma_bf16(dt, ad, bd, idesc, ((kb - kb0) | j | kk) != 0);
               if (SPLIT != 1) {
                 umma_bf16(dt, ad, sdesc_k_sw128(b_hi + C::B_BYTES + kk * 32), idesc, 1);
                 umma_bf16(dt, sdesc_k_sw128(a_hi + C::A_BYTES + kk * 32), bd, idesc, 1);
@@ -1055,9 +1082,10 @@ __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ desc
         get_tile(descs, tiles, t, p, tm, tn);
         const GemmDesc& d = descs[p];
         const int nk = (d.s.K + BK - 1) / BK;
+        const int kb0 = first_kblock(d.s, tm * PBM, BK);
         const int half = d.s.bn / 2;
         const uint32_t bytes = 2u * (uint32_t)(C::A_BYTES + half * BK * 2);  // both CTAs' copies
-        for (int kb = 0; kb < nk; ++kb, ++g) {
+        for (int kb = kb0; kb < nk; ++kb, ++g) {
           const int s = g % STAGES;
           const uint32_t ph = (g / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, abort)) break;
@@ -1092,13 +1120,14 @@ __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ desc
         get_tile(descs, tiles, t, p, tm, tn);
         const GemmDesc& d = descs[p];
         const int nk = (d.s.K + BK - 1) / BK;
+        const int kb0 = first_kblock(d.s, tm * PBM, BK);
         const uint32_t acc = i & 1, aph = (i >> 1) & 1;
         if (!mbar_wait(&tempty[acc], aph ^ 1, abort)) break;
         tc_fence_after();
         const uint32_t dt = tmem_base + acc * BNMAX;
         const uint32_t idesc = idesc_bf16_m256(d.s.bn);
         bool ok = true;
-        for (int kb = 0; kb < nk; ++kb, ++g) {
+        for (int kb = kb0; kb < nk; ++kb, ++g) {
           const int s = g % STAGES;
           const uint32_t ph = (g / STAGES) & 1;
           if (!mbar_wait(&full[s], ph, abort)) {
@@ -1110,7 +1139,7 @@ __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ desc
           const uint32_t b0 = a0 + C::A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
-            umma_bf16_pair(dt, sdesc_k_sw128(a0 + kk * 32), sdesc_k_sw128(b0 + kk * 32), idesc, (kb | kk) != 0);
+            umma_bf16_pair(dt, sdesc_k_sw128(a0 + kk * 32), sdesc_k_sw128(b0 + kk * 32), idesc, ((kb - kb0) | kk) != 0);
           issued = true;
           umma_commit_pair(&empty[s], 3);
         }
@@ -1225,7 +1254,9 @@ static int check_spec(const PsgdGemmSpec& s, int split) {
   if (s.M < 1 || s.N < 1 || s.K < 1 || !valid_bn(s.bn, split)) return PSGD_EINVAL;
   if (split == 3 && (s.a_lo == nullptr || s.b_lo == nullptr)) return PSGD_EINVAL;
   if (s.mode == PSGD_GEMM_SYRK && (s.M != s.N || s.bn < 128)) return PSGD_EINVAL;
-  if (s.mode != PSGD_GEMM_PLAIN && s.mode != PSGD_GEMM_SYRK) return PSGD_EINVAL;
+  if (s.mode == PSGD_GEMM_TRMM && s.M != s.K) return PSGD_EINVAL;
+  if (s.mode != PSGD_GEMM_PLAIN && s.mode != PSGD_GEMM_SYRK && s.mode != PSGD_GEMM_TRMM) return PSGD_EINVAL;
+  if (s.out_packed && s.mode != PSGD_GEMM_SYRK) return PSGD_EINVAL;
   if (s.cs_mode && (s.cs_nf == nullptr || (s.cs_mode == 2 && (s.cs_part == nullptr || s.cs_T < 1)))) return PSGD_EINVAL;
   if (s.M > 65535 * BM || s.N > 65535 * s.bn) return PSGD_EINVAL;
   return PSGD_OK;
@@ -1478,7 +1509,7 @@ extern "C" int psgd_gemm_count_tiles(const PsgdGemmSpec* specs, int nspecs) {
 // is several times dearer than the specialised ones). The accumulators are double-buffered, so the two overlap.
 static double tile_cost(const GemmDesc& d, int tm, int tn, int kind, int bm) {
   const PsgdGemmSpec& s = d.s;
-  const double nk = (double)((s.K + BK - 1) / BK);
+  const double nk = (double)((s.K + BK - 1) / BK - first_kblock(s, (long long)tm * bm, BK));
   const double mma = nk * 730.0 * (s.bn / 256.0) * ((s.a_lo && s.b_lo) ? 3.0 : 1.0) + 1500.0;
   const long long m0 = (long long)tm * bm, n0 = (long long)tn * s.bn;
   const bool interior = m0 + bm <= s.M && n0 + s.bn <= s.N;

@@ -884,6 +884,9 @@ __global__ void __launch_bounds__(256, LO ? 2 : 3) trace_kernel(const PsgdTraceI
 }
 
 // ---- clip + apply ------------------------------------------------------------------------------------------------
+// torch.clamp(x, -me, me) (psgd_pro.py:380): NaN stays NaN (fminf / fmaxf alone would drop it), +-Inf clamps.
+__device__ __forceinline__ float clip_elem(float x, float me) { return isnan(x) ? x : fminf(fmaxf(x, -me), me); }
+
 __global__ void __launch_bounds__(256) clip_scale_kernel(const PsgdApplyItem* __restrict__ items,
                                                         const float* __restrict__ hyper) {
   const PsgdApplyItem& it = items[blockIdx.x];
@@ -893,8 +896,10 @@ __global__ void __launch_bounds__(256) clip_scale_kernel(const PsgdApplyItem* __
   const float tot = block_sum(s, red);
   if (threadIdx.x == 0) {
     const float avg = sqrtf(tot / (float)it.numel);
-    // clamp(max_avg / avg, max = 1): exactly 1 when the reference's branch would not fire
-    *it.scale = fminf(hyper[PSGD_HY_MAX_AVG] / avg, 1.f);
+    // psgd_pro.py:374-376: the scale is max_avg / avg only when avg > max_avg (a NaN avg leaves it 1, as the
+    // reference's comparison does; an infinite avg gives 0, and Inf * 0 = NaN then reaches the parameter)
+    const float max_avg = hyper[PSGD_HY_MAX_AVG];
+    *it.scale = avg > max_avg ? max_avg / avg : 1.f;
   }
 }
 
@@ -915,7 +920,7 @@ __global__ void __launch_bounds__(256) apply_kernel(const PsgdApplyItem* __restr
         const float4 g4 = *reinterpret_cast<const float4*>(it.pg + k);
         float g[4] = {g4.x, g4.y, g4.z, g4.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) g[i] = fminf(fmaxf(g[i] * sc, -me), me);
+        for (int i = 0; i < 4; ++i) g[i] = clip_elem(g[i] * sc, me);
         if (it.param_bf16) {
           uint2* pp = reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(it.param) + k);
           uint2 u = *pp;
@@ -931,7 +936,7 @@ __global__ void __launch_bounds__(256) apply_kernel(const PsgdApplyItem* __restr
         }
       }
       for (long long k = vend + threadIdx.x; k < end; k += blockDim.x) {
-        const float g = fminf(fmaxf(it.pg[k] * sc, -me), me);
+        const float g = clip_elem(it.pg[k] * sc, me);
         if (it.param_bf16) {
           __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(it.param);
           p[k] = __float2bfloat16_rn(__bfloat162float(p[k]) - lr * g);
@@ -943,7 +948,7 @@ __global__ void __launch_bounds__(256) apply_kernel(const PsgdApplyItem* __restr
       continue;
     }
     for (long long k = base + threadIdx.x; k < end; k += blockDim.x) {
-      const float g = fminf(fmaxf(it.pg[k] * sc, -me), me);
+      const float g = clip_elem(it.pg[k] * sc, me);
       if (it.param_bf16) {
         __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(it.param);
         p[k] = __float2bfloat16_rn(__bfloat162float(p[k]) - lr * g);

@@ -43,7 +43,7 @@ def split_into(x, hi, lo):
 def make_spec(a, b, M, N, K, bn=128, mode=PSGD_GEMM_PLAIN, alpha=1.0, beta=0.0, alpha_ptr=None, beta_ptr=None,
               aux=None, row_scale=None, col_scale=None, out_f32=None, out_hi=None, out_lo=None, out_hi_t=None,
               out_lo_t=None, part_tile=None, part_col=None, part_row=None, diag_out=None, dot_aux=None,
-              part_dot=None, cs_part=None, cs_T=0, cs_mode=0, cs_nf=None):
+              part_dot=None, cs_part=None, cs_T=0, cs_mode=0, cs_nf=None, out_packed=None):
     """GemmSpec for D = A B^T with a = (a_hi, a_lo), b = (b_hi, b_lo) bf16 operands (lo may be None)."""
     a_hi, a_lo = a
     b_hi, b_lo = b
@@ -63,6 +63,7 @@ def make_spec(a, b, M, N, K, bn=128, mode=PSGD_GEMM_PLAIN, alpha=1.0, beta=0.0, 
     s.part_tile, s.part_col, s.part_row, s.diag_out = ptr(part_tile), ptr(part_col), ptr(part_row), ptr(diag_out)
     s.dot_aux, s.ld_dot, s.part_dot = ptr(dot_aux), (dot_aux.stride(0) if dot_aux is not None else 0), ptr(part_dot)
     s.cs_part, s.cs_T, s.cs_mode, s.cs_nf = ptr(cs_part), cs_T, cs_mode, ptr(cs_nf)
+    s.out_packed = ptr(out_packed)
     return s
 
 
@@ -101,8 +102,9 @@ class GemmGroup:
                                            self.kind, ptr(err), stream_handle()), "psgd_gemm_launch")
 
 
-def _prep_one(item_fields, rows, cols, normal):
-    """One psgd_prep launch for a single item (plug-in helpers; item and work list uploaded per call)."""
+def _prep_one(item_fields, rows, cols, normal, err=None):
+    """One psgd_prep launch for a single item (plug-in helpers; item and work list uploaded per call). err: the
+    device error word to report into (a fresh one when None)."""
     it = _capi.PrepItem()
     for k, v in item_fields.items():
         setattr(it, k, v)
@@ -116,18 +118,19 @@ def _prep_one(item_fields, rows, cols, normal):
         pairs = [(0, (ti << 16) | tj) for ti in range((rows + 31) // 32) for tj in range((cols + 31) // 32)]
     work = torch.tensor([v for p in pairs for v in p], dtype=torch.int32).to(dev)
     hyper = torch.zeros(_capi.HY_COUNT, device=dev)
-    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    if err is None:
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
     check(_capi.lib().psgd_prep(items.data_ptr(), work.data_ptr(), len(pairs), hyper.data_ptr(), err.data_ptr(),
                                 stream_handle()), "psgd_prep")
     return (items, work, hyper, err)  # kept alive by the caller until the launch has run
 
 
-def to_operand(X, transpose=False, split=True):
+def to_operand(X, transpose=False, split=True, err=None):
     """(hi, lo) bf16 operand of the fp32 / bf16 matrix X (or of X^T), staged by the psgd_prep kernel."""
     X = X.contiguous()
     r, c = X.shape
     hi, lo = operand(c, r, X.device, split) if transpose else operand(r, c, X.device, split)
     keep = _prep_one(dict(g=X.data_ptr(), g_bf16=int(X.dtype == BF16), mode=_capi.PSGD_PREP_TRANS if transpose
                           else _capi.PSGD_PREP_NORMAL, xi=None, n1=r, n2=c, p1=None, p2=None, out_hi=ptr(hi),
-                          out_lo=ptr(lo), ld_out=hi.stride(0), eps=0.0), r, c, not transpose)
+                          out_lo=ptr(lo), ld_out=hi.stride(0), eps=0.0), r, c, not transpose, err)
     return (hi, lo), keep

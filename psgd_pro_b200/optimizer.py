@@ -45,6 +45,13 @@ def is_dense(size, numel, max_size, max_skew):
     return not (size <= 1 or size > max_size or size ** 2 > max_skew * numel)
 
 
+def init_scale_from_grads(grads, damping):
+    """psgd_pro.py:329-332: (max_i mean|g_i|^4 + damping^4)^(-1/8), accumulated in float64 (a one-time reduction;
+    a sharded step takes it over every parameter's gradient on every rank, so all ranks agree bit for bit)."""
+    m = max(float(torch.mean(g.detach().to(torch.float64).abs() ** 4)) for g in grads)
+    return (m + damping ** 4) ** (-1 / 8)
+
+
 def cdiv(a, b):
     return (a + b - 1) // b
 
@@ -618,12 +625,27 @@ class KronWhiten:
     (lr_params, lr_preconditioner, betaL, damping, momentum, grad_clip_max_amps,
     preconditioner_update_probability, update_preconditioner_first), step(closure) and step_math(grads) of
     psgd_pro_fast.py:440-499. Extra keyword arguments: precision ("fp32", "bf16" or None = from the parameter
-    dtype) and cuda_graphs (capture the step after the first call)."""
+    dtype) and cuda_graphs (capture the step after the first call).
+
+    The keyword arguments psgd_pro_fast.KronWhiten adds (psgd_pro_fast.py:245-264) are accepted, so its callers
+    drop in; the B200 step subsumes what they select, and the two argument checks of the reference are kept:
+      compile    (None, a torch.compile mode or options): the step is captured in CUDA graphs whatever the value;
+      ops        (EagerOps or a kernel class): the dense-factor arithmetic always runs in this package's kernels;
+      batch      same-shape parameters always share one grouped launch per phase (no vmap stacking);
+      cache_p, p2d   P_i = Q_i^T Q_i is always kept as state between steps (psgd_pro_fast.py:164-192);
+      graph_rng  the damping noise is always generated on the device (in the staging kernel);
+      r2         the Procrustes step always takes the one-product form of psgd_pro_fast.py:141-153 (r2=False selects
+                 the two-product form of :129-138 there; the two differ in rounding only)."""
 
     def __init__(self, params_with_grad, preconditioner_max_size=float("inf"), preconditioner_max_skew=1.0,
                  preconditioner_init_scale=None, lr_params=0.001, lr_preconditioner=0.1, betaL=0.9, damping=1e-9,
                  momentum=0.0, grad_clip_max_amps=(2.0, 10.0), preconditioner_update_probability=1.0,
-                 update_preconditioner_first=True, whiten_grad=True, precision=None, cuda_graphs=True):
+                 update_preconditioner_first=True, whiten_grad=True, compile=None, ops=None, batch=False,
+                 cache_p=False, graph_rng=False, p2d=False, r2=False, precision=None, cuda_graphs=True):
+        # psgd_pro_fast.py:289, :294: the reference's own argument checks
+        assert not (cache_p and compile is not None), "cache_p relies on tensor version counters: eager only"
+        assert not (p2d and batch), "p2d keeps per-parameter P state; batch stacks parameters"
+        self.ops = ops  # kept for callers that read it back; the arithmetic does not go through it
         self.lr_params = lr_params
         self.lr_preconditioner = lr_preconditioner
         self.betaL = betaL
@@ -675,6 +697,14 @@ class KronWhiten:
                      betaL=self.betaL, damping=self.damping, momentum=self.momentum,
                      grad_clip_max_amps=self.grad_clip_max_amps,
                      preconditioner_update_probability=self.preconditioner_update_probability)]
+
+    def set_init_scale(self, scale):
+        """Initialises the preconditioner with Q factors scale^(1/order) I (psgd_pro.py:181, :210) before the first
+        step, as preconditioner_init_scale would; used when the scale comes from gradients this optimizer does
+        not see (a rank of a sharded step takes it over every parameter's gradient, psgd_pro.py:329-332)."""
+        if self._plan is not None:
+            raise RuntimeError("the preconditioner is already initialised")
+        self._build(float(scale))
 
     def _build(self, scale):
         shapes = [tuple(p.squeeze().shape) for p in self._params_with_grad]
@@ -780,9 +810,7 @@ class KronWhiten:
                 raise ValueError("gradients must be fp32 or bf16 tensors on the parameters' device")
         grads = [g if g.is_contiguous() else g.contiguous() for g in grads]
         if self._plan is None:
-            scale = max(float(torch.mean(g.float().abs() ** 4)) for g in grads)  # psgd_pro.py:330-331
-            scale = (scale + self.damping ** 4) ** (-1 / 8)
-            self._build(scale)
+            self._build(init_scale_from_grads(grads, self.damping))
         plan = self._plan
         beta = 0.0
         if self.momentum > 0:  # psgd_pro.py:334-343

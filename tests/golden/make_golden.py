@@ -10,7 +10,11 @@ tests/test_oracle_golden.py replays the same stream into the oracle (oracle/psgd
 
 Scenario parameters, gradients and draws are all derived from the seed; each .npz stores the scenario metadata
 (json) and the reference's state after the last step: Q factors, L, parameters and the last preconditioned
-gradients (before clipping)."""
+gradients (before clipping). Scenarios marked "sketch" (the large bf16 case of the benchmarked path) store
+two-sided sketches of the matrices instead (tests/golden/sketch.py), and the parameter change instead of the
+parameter; "grad_bf16" scenarios round every gradient to bf16 values, which the reference then sees as fp32.
+
+    python tests/golden/make_golden.py /path/to/reference [scenario names ...]   (default: all)"""
 import json
 import os
 import sys
@@ -20,6 +24,9 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("PSGD_REFERENCE", "")
+ONLY = set(sys.argv[2:])
+sys.path.insert(0, HERE)
+from sketch import sketch  # noqa: E402
 
 SCENARIOS = [
     # config 1 of the benchmark plan: one fp32 256 x 512 weight, both factors dense, 10 steps
@@ -41,6 +48,13 @@ SCENARIOS = [
     dict(name="prob_half", shapes=[[32, 16]], steps=6, grad_scale=[1e-2], seed=4,
          kw=dict(preconditioner_update_probability=0.5, preconditioner_max_skew=float("inf"),
                  preconditioner_init_scale=1.0)),
+    # the benchmarked path at its own sizes: the factor sizes of the Llama-style set (2048, 256, 5632), a 1-D 2048
+    # parameter and an embedding whose 32000 dim exceeds max size 8192 (a diagonal factor); gradients N(0, 1e-3^2)
+    # rounded to bf16 values, the init scale taken on the fly, max_skew = inf
+    dict(name="llama_block_bf16", shapes=[[2048, 2048], [256, 2048], [5632, 2048], [2048, 5632], [2048],
+                                          [32000, 2048]], steps=3,
+         grad_scale=[1e-3] * 6, seed=5, sketch=True, grad_bf16=True,
+         kw=dict(preconditioner_max_size=8192, preconditioner_max_skew=float("inf"))),
 ]
 
 
@@ -81,9 +95,17 @@ def torch_proxy(real, server):
     return mod
 
 
-def grads_for(rng, shapes, scales):
-    return [np.asarray(rng.standard_normal(tuple(s), dtype=np.float32) * np.float32(sc), dtype=np.float32)
-            for s, sc in zip(shapes, scales)]
+def grads_for(rng, shapes, scales, bf16=False):
+    out = [np.asarray(rng.standard_normal(tuple(s), dtype=np.float32) * np.float32(sc), dtype=np.float32)
+           for s, sc in zip(shapes, scales)]
+    return [to_bf16_values(g) for g in out] if bf16 else out
+
+
+def to_bf16_values(x):
+    """float32 array rounded to the nearest bf16 value (round to nearest even), still float32."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    r = ((u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xFFFF0000)).astype(np.uint32)
+    return r.view(np.float32)
 
 
 def run_scenario(sc, torch, psgd_pro):
@@ -134,7 +156,7 @@ def run_scenario(sc, torch, psgd_pro):
             step_box[0] = step
             state["param_idx"] = 0
             captured["pre"] = []
-            G = grads_for(rng_grads, sc["shapes"], sc["grad_scale"])
+            G = grads_for(rng_grads, sc["shapes"], sc["grad_scale"], sc.get("grad_bf16", False))
 
             def closure():
                 return sum((p * torch.from_numpy(g)).sum() for p, g in zip(params, G))
@@ -142,13 +164,20 @@ def run_scenario(sc, torch, psgd_pro):
     finally:
         psgd_pro.torch = real_torch
     out = {}
+    sk = sc.get("sketch", False)
+    keep = (lambda x: sketch(x)) if sk else (lambda x: np.asarray(x, dtype=np.float32))
+    rng_p0 = np.random.default_rng(1000 + sc["seed"])
     for k, (QL, _) in enumerate(opt._QLs_exprs):
         Q, L = QL
         for i, q in enumerate(Q):
-            out[f"Q_{k}_{i}"] = q.detach().numpy().astype(np.float32)
+            out[f"Q_{k}_{i}"] = keep(q.detach().numpy())
             out[f"L_{k}_{i}"] = np.float32(L[i].item())
-        out[f"param_{k}"] = params[k].detach().numpy().astype(np.float32)
-        out[f"pre_{k}"] = captured["pre"][k].numpy().astype(np.float32)
+        p0 = np.asarray(rng_p0.standard_normal(tuple(sc["shapes"][k]), dtype=np.float32))
+        if sk:
+            out[f"dparam_{k}"] = sketch(params[k].detach().numpy().astype(np.float64) - p0)
+        else:
+            out[f"param_{k}"] = params[k].detach().numpy().astype(np.float32)
+        out[f"pre_{k}"] = keep(captured["pre"][k].numpy())
     meta = dict(sc)
     meta["kw"] = {k: (v if v != float("inf") else "inf") for k, v in sc["kw"].items()}
     meta["force_balance"] = {str(k): v for k, v in sc.get("force_balance", {}).items()}
@@ -222,12 +251,16 @@ def main():
     import psgd_pro
     import psgd_pro_fast as fast
     for sc in SCENARIOS:
+        if ONLY and sc["name"] not in ONLY:
+            continue
         out = run_scenario(sc, torch, psgd_pro)
         np.savez_compressed(os.path.join(HERE, sc["name"] + ".npz"), **out)
         print("wrote", sc["name"], sum(v.size for v in out.values()), "values")
-    np.savez_compressed(os.path.join(HERE, "fast_r2.npz"), **run_fast_r2(torch, fast))
-    np.savez_compressed(os.path.join(HERE, "units.npz"), **run_units(torch, psgd_pro, fast))
-    print("wrote fast_r2, units")
+    if not ONLY or "fast_r2" in ONLY:
+        np.savez_compressed(os.path.join(HERE, "fast_r2.npz"), **run_fast_r2(torch, fast))
+    if not ONLY or "units" in ONLY:
+        np.savez_compressed(os.path.join(HERE, "units.npz"), **run_units(torch, psgd_pro, fast))
+    print("done")
 
 
 if __name__ == "__main__":

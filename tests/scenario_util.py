@@ -47,6 +47,35 @@ def reference_order_draws(rng, QL, shapes, prob, forced):
     return d
 
 
+class _FactorShape:
+    """Stands in for a Q factor where only its kind matters (ndim 2: dense n x n, ndim 1: diagonal)."""
+
+    def __init__(self, n, dense):
+        self.ndim, self.shape = (2 if dense else 1), ((n, n) if dense else (n,))
+
+
+def factor_layout(shapes, max_size, max_skew):
+    """(Q list, L list) stand-ins with the dense / diagonal kinds of psgd_pro.py:189, for drawing the reference-order
+    random stream without building the factors (the oracle's init_kron would allocate every n x n identity)."""
+    out = []
+    for shp in shapes:
+        shp = tuple(shp)
+        if len(shp) == 0:
+            out.append(([_FactorShape(1, False)], [0.0]))
+            continue
+        numel = int(np.prod(shp))
+        out.append(([_FactorShape(n, O.is_dense(n, numel, max_size, max_skew)) for n in shp], [0.0] * len(shp)))
+    return out
+
+
+def to_bf16_values(x):
+    """float32 array rounded to the nearest bf16 value (round to nearest even), still float32; the rounding
+    tests/golden/make_golden.py applies to the gradients of its grad_bf16 scenarios."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    r = ((u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xFFFF0000)).astype(np.uint32)
+    return r.view(np.float32)
+
+
 class Scenario:
     """Parameters, per-step gradients and draws of a golden scenario, in the reference order."""
 
@@ -61,8 +90,9 @@ class Scenario:
 
     def grads(self):
         m = self.meta
-        return [np.asarray(self.rng_grads.standard_normal(tuple(s), dtype=np.float32) * np.float32(sc),
-                           dtype=np.float32) for s, sc in zip(m["shapes"], m["grad_scale"])]
+        out = [np.asarray(self.rng_grads.standard_normal(tuple(s), dtype=np.float32) * np.float32(sc),
+                          dtype=np.float32) for s, sc in zip(m["shapes"], m["grad_scale"])]
+        return [to_bf16_values(g) for g in out] if m.get("grad_bf16") else out
 
     def draws(self, step, QL, grads):
         shapes = [np.squeeze(x).shape for x in grads]

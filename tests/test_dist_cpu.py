@@ -24,44 +24,59 @@ class OracleOptimizer:
         self.params = params
         self.o = O.KronWhitenOracle([p.detach().numpy().copy() for p in params], dtype=np.float64, **kw)
 
+    def set_init_scale(self, scale):
+        self.o.QL = [O.init_kron(np.squeeze(p).shape, scale, self.o.max_size, self.o.max_skew, self.o.dtype)
+                     for p in self.o.params]
+
     def step_math(self, grads, draws=None):
         self.o.step([g.numpy() for g in grads], draws)
         for p, new in zip(self.params, self.o.params):
             p.data.copy_(torch.from_numpy(np.asarray(new, dtype=np.float32)).reshape(p.shape))
 
 
-def make_inputs(steps=3):
+KW_ONTHEFLY = dict(KW, preconditioner_init_scale=None)
+
+
+def make_inputs(steps=3, kw=KW):
     rng = np.random.default_rng(0)
     p0 = [rng.standard_normal(s).astype(np.float32) for s in SHAPES]
-    G = [[(rng.standard_normal(s) * 0.02).astype(np.float32) for s in SHAPES] for _ in range(steps)]
-    ora = O.KronWhitenOracle(p0, dtype=np.float64, **KW)
+    # gradient scales differ per parameter, so the on-the-fly init scale (a max over all gradients) depends on
+    # which rank sees which gradient unless every rank takes the max over all of them
+    G = [[(rng.standard_normal(s) * 0.02 * (1 + k)).astype(np.float32) for k, s in enumerate(SHAPES)]
+         for _ in range(steps)]
+    ora = O.KronWhitenOracle(p0, dtype=np.float64, **kw)
     D = [ora.make_draws(rng, g, coins=[1.0] * len(SHAPES)) for g in G]
     for d in D:
         d["update"] = 0.0
     return p0, G, D
 
 
-def single_process_result():
-    p0, G, D = make_inputs()
-    ora = O.KronWhitenOracle(p0, dtype=np.float64, **KW)
+def single_process_result(kw=KW):
+    p0, G, D = make_inputs(kw=kw)
+    ora = O.KronWhitenOracle(p0, dtype=np.float64, **kw)
     for g, d in zip(G, D):
         ora.step(g, d)
     return [np.asarray(p, dtype=np.float32) for p in ora.params]
 
 
-def worker(rank, world, port, flat, out):
+def worker(rank, world, port, flat, out, kw=KW, buckets=1):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        p0, G, D = make_inputs()
+        p0, G, D = make_inputs(kw=kw)
         owner = assignment_for(SHAPES, world, max_skew=float("inf"))
         if flat:
-            params, buf, seg = make_flat_params(SHAPES, owner, world, torch.float32, "cpu",
-                                                init=lambda s, it=iter(p0): torch.from_numpy(next(it)))
-            opt = ShardedKronWhiten(params, assignment=owner, flat=(buf, seg), optimizer_factory=OracleOptimizer, **KW)
+            it = iter(p0)
+            params, buf, layout = make_flat_params(SHAPES, owner, world, torch.float32, "cpu",
+                                                   init=lambda s: torch.from_numpy(next(it)), buckets=buckets,
+                                                   max_skew=float("inf"))
+            opt = ShardedKronWhiten(params, assignment=owner, flat=(buf, layout), optimizer_factory=OracleOptimizer,
+                                    **kw)
         else:
             params = [torch.nn.Parameter(torch.from_numpy(p.copy())) for p in p0]
-            opt = ShardedKronWhiten(params, assignment=owner, optimizer_factory=OracleOptimizer, **KW)
+            opt = ShardedKronWhiten(params, assignment=owner, optimizer_factory=OracleOptimizer, buckets=buckets,
+                                    **kw)
+        assert 1 <= opt.nbuckets <= buckets
         for g, d in zip(G, D):
             opt.step_math([torch.from_numpy(x) for x in g], draws=d)
         out[rank] = [p.detach().numpy().copy() for p in params]
@@ -69,13 +84,18 @@ def worker(rank, world, port, flat, out):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("flat", [False, True])
-def test_sharded_step_matches_one_process(flat):
-    ref = single_process_result()
+@pytest.mark.parametrize("flat,onthefly,buckets", [(False, False, 1), (True, False, 1), (True, True, 1),
+                                                    (True, False, 3), (False, True, 2)])
+def test_sharded_step_matches_one_process(flat, onthefly, buckets):
+    """onthefly: no preconditioner_init_scale, so the first step sets it from max_i mean|g_i|^4 over every
+    parameter's gradient (psgd_pro.py:329-332), on every rank alike. buckets: each rank's parameters stepped and
+    all-gathered in that many buckets."""
+    kw = KW_ONTHEFLY if onthefly else KW
+    ref = single_process_result(kw)
     mgr = mp.Manager()
     out = mgr.dict()
-    port = 29500 + (os.getpid() % 500) + (7 if flat else 0)
-    mp.spawn(worker, args=(2, port, flat, out), nprocs=2, join=True)
+    port = 29500 + (os.getpid() % 400) + (7 if flat else 0) + (13 if onthefly else 0) + 31 * buckets
+    mp.spawn(worker, args=(2, port, flat, out, kw, buckets), nprocs=2, join=True)
     for r in range(2):
         for a, b in zip(out[r], ref):
             np.testing.assert_array_equal(a, b)

@@ -25,3 +25,20 @@ def test_make_ops_surface():
     for m in ("gram", "gram_q", "norm_lower_bound_spd", "norm_lower_bound_skh", "symm", "symm_r", "syrk", "sym"):
         assert callable(getattr(O, m))
     assert "b200" in O.flags and ops.side(torch.empty(55)) == 10
+
+
+def test_kronwhiten_accepts_the_fast_class_keywords():
+    """psgd_pro_fast.KronWhiten's constructor (psgd_pro_fast.py:245-264) takes these keywords beyond psgd_pro's;
+    callers that pass them must drop in unchanged."""
+    import inspect
+    from psgd_pro_b200 import KronWhiten
+    sig = inspect.signature(KronWhiten.__init__).parameters
+    fast_kw = dict(preconditioner_max_size=float("inf"), preconditioner_max_skew=1.0, preconditioner_init_scale=None,
+                   lr_params=0.001, lr_preconditioner=0.1, betaL=0.9, damping=1e-9, momentum=0.0,
+                   grad_clip_max_amps=(2.0, 10.0), preconditioner_update_probability=1.0,
+                   update_preconditioner_first=True, whiten_grad=True, compile=None, batch=False, cache_p=False,
+                   graph_rng=False, p2d=False, r2=False)
+    for k, v in fast_kw.items():
+        assert k in sig, k
+        assert sig[k].default == v, (k, sig[k].default, v)
+    assert "ops" in sig

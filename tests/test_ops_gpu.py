@@ -21,7 +21,7 @@ def g():
     return torch.Generator().manual_seed(0)
 
 
-@pytest.mark.parametrize("shape", [(96, 200), (65, 10), (256, 512), (3, 130)])
+@pytest.mark.parametrize("shape", [(96, 200), (65, 10), (256, 512), (3, 130), (640, 300)])
 def test_syrk_both_orientations(cuda, g, shape):
     X = torch.randn(shape, generator=g).to(cuda)
     for trans in (False, True):
@@ -36,6 +36,9 @@ def test_syrk_both_orientations(cuda, g, shape):
         i, j = 3 % n, (n - 1)
         assert abs(P[i * n - i * (i - 1) // 2 + j - i].item() - ref[i, j].item()) <= 1e-4 * ref.abs().max().item()
         assert rel(ops.unpack(P, n), ref) < TOL
+        # every packed entry (the fast epilogue writes interior tiles, the general one the edges and diagonal)
+        iu = torch.triu_indices(n, n)
+        assert rel(P.cpu(), ref[iu[0], iu[1]]) < TOL
 
 
 @pytest.mark.parametrize("n,p", [(128, 64), (65, 33), (300, 7)])
@@ -94,3 +97,57 @@ def test_eager_ops_contract(cuda, g):
     assert rel(Ops.syrk(Pg, True), Pg.double().T @ Pg.double()) < TOL
     Pk = ops.make_ops({"packed"}).sym(Pg, False)
     assert Pk.dim() == 1 and rel(ops.unpack(Pk, 64), Pg.double() @ Pg.double().T) < TOL
+
+
+def poison_lower(M):
+    """The square form of kernels/ops.py:190: the lower triangle holds NaN, which no kernel may read."""
+    T = M.clone()
+    n = T.shape[0]
+    T[torch.ones(n, n, dtype=torch.bool, device=T.device).tril(-1)] = float("nan")
+    return T
+
+
+def packed(M):
+    n = M.shape[0]
+    iu = torch.triu_indices(n, n, device=M.device)
+    return M[iu[0], iu[1]].contiguous()
+
+
+@pytest.mark.parametrize("n", [1, 64, 130, 513])
+@pytest.mark.parametrize("sign", [1, -1])
+def test_storage_forms_kernels(cuda, g, n, sign):
+    """tri_vmm, tri_rownorm2, unpack and the norm bounds from the square-upper and packed forms, lower half
+    poisoned; the skew form has a zero diagonal (kernels/k1.cu:41-50)."""
+    A = torch.randn(n, n, generator=g)
+    full = (A + A.T) if sign > 0 else (A - A.T)
+    full = full.to(cuda)
+    V = torch.randn(32, n, generator=g).to(cuda)
+    for form in (poison_lower(full), packed(full)):
+        W = ops.tri_vmm(V, form, sign)
+        assert rel(W, V.double() @ full.double()) < TOL
+        if sign > 0:
+            r, m = ops.tri_rownorm2(form)
+            F = full.double()
+            assert rel(r, (F * F).sum(1)) < 1e-6 and abs(m.item() - F.abs().max().item()) <= 1e-6 * F.abs().max().item()
+    assert torch.equal(ops.unpack(packed(full), n).cpu(), full.cpu()) if sign > 0 else True
+    if n >= 2:
+        bound = (ops.norm_lower_bound_spd if sign > 0 else ops.norm_lower_bound_skh)
+        ora = (O.norm_lower_bound_spd if sign > 0 else O.norm_lower_bound_skh)
+        M = full @ full.T if sign > 0 else full  # an spd matrix for the spd bound
+        want = ora(M.double().cpu().numpy(), V.cpu().numpy())
+        got_sq = bound(poison_lower(M), V).item()
+        got_pk = bound(packed(M), V).item()
+        assert abs(got_sq / want - 1) < 1e-4 and abs(got_pk / want - 1) < 1e-4
+    ops.check_errors()
+
+
+@pytest.mark.parametrize("n,p", [(128, 64), (300, 7), (1024, 512)])
+def test_trmm_skips_the_zero_triangle(cuda, g, n, p):
+    """triu(T) @ X (the triangular-times-dense product of the benchmark plan; oracle torch.triu(T) @ X in fp64)
+    with the lower triangle of T poisoned: it is neither read nor multiplied."""
+    T = torch.randn(n, n, generator=g) / n ** 0.5 + torch.eye(n)
+    X = torch.randn(n, p, generator=g)
+    ref = torch.triu(T).double() @ X.double()
+    C = ops.trmm_impl(poison_lower(T.to(cuda)), X.to(cuda))
+    assert rel(C, ref) < TOL
+    ops.check_errors()

@@ -36,6 +36,24 @@ def test_oracle_matches_reference(name, dtype):
         assert rel(pre[k], g[f"pre_{k}"]) < tol, (name, k, rel(pre[k], g[f"pre_{k}"]))
 
 
+def test_oracle_matches_reference_at_benchmark_sizes():
+    """The benchmarked path's sizes (llama_block_bf16: factors of 2048, 256 and 5632, a 1-D 2048 parameter, a
+    32000 x 2048 embedding with a diagonal factor; bf16 gradient values; init scale on the fly): the fp32 oracle
+    against the reference's own outputs, stored as sketches (tests/golden/sketch.py). About a minute of CPU."""
+    import sys
+    import os
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+    from sketch import sketch
+    g, opt, pre = replay("llama_block_bf16", np.float32)
+    errs = {}
+    for k, (Q, L) in enumerate(opt.QL):
+        for i, q in enumerate(Q):
+            errs[f"Q_{k}_{i}"] = rel(sketch(q), g[f"Q_{k}_{i}"])
+            assert abs(L[i] - float(g[f"L_{k}_{i}"])) <= 1e-5 * abs(float(g[f"L_{k}_{i}"]))
+        errs[f"pre_{k}"] = rel(sketch(pre[k]), g[f"pre_{k}"])
+    assert max(errs.values()) < 1e-5, errs  # measured: Q ~1e-7, Pg ~1.5e-6
+
+
 def test_fast_r2_paths():
     """oracle update_precond (r2 False/True) against psgd_pro_fast.update_2d on the same draws."""
     g = load("fast_r2")

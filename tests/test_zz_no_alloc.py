@@ -53,6 +53,18 @@ def apply_with_caller_scratch(param, pg):
     assert err.item() == 0
 
 
+def reference_apply(p0, pg):
+    """psgd_pro.py:371-381 restated in fp32 torch: scale Pg to RMS max_avg_amp when its RMS is larger, clamp each
+    element to +-max_element_amp, param -= lr_params * Pg (a bf16 parameter is updated in fp32 and rounded back,
+    as torch's subtract_ on a bf16 tensor does)."""
+    g = pg.clone()
+    avg = torch.sqrt(torch.mean(g * g))
+    if avg > MAX_AVG:
+        g *= MAX_AVG / avg
+    g.clamp_(min=-MAX_ELEM, max=MAX_ELEM)
+    return (p0.float() - LR * g).to(p0.dtype)
+
+
 def apply_without_scratch(param, pg):
     rc = _capi.lib().psgd_apply_noalloc(param.data_ptr(), int(param.dtype == torch.bfloat16), pg.data_ptr(),
                                         pg.numel(), LR, MAX_AVG, MAX_ELEM, stream_handle())
@@ -78,6 +90,12 @@ def test_noalloc_matches_apply_on_two_calls_in_a_row(cuda, dtype):
         assert torch.isfinite(b.float()).all()
         assert rel(b.float() - p0.float(), a.float() - p0.float()) < 1e-3
         assert rel(b.float(), a.float()) < 1e-3
+        # and directly against the reference's arithmetic (fp32 torch); a bf16 parameter may differ by one rounding
+        # of the stored value where the two fp32 results straddle a bf16 rounding boundary
+        r = reference_apply(p0, pg)
+        bar = 1e-3 if dtype == torch.float32 else 2e-2
+        assert rel(b.float() - p0.float(), r.float() - p0.float()) < bar
+        assert rel(b.float(), r.float()) < 1e-3
         # the update really was clipped / clamped as the reference does (psgd_pro.py:371-381)
         step = (p0.float() - b.float()) / LR
         assert step.abs().max().item() <= MAX_ELEM * 1.01
@@ -90,3 +108,20 @@ def test_noalloc_rejects_sizes_beyond_its_scratch(cuda):
     rc = lib.psgd_apply_noalloc(x.data_ptr(), 0, x.data_ptr(), too_big, LR, MAX_AVG, MAX_ELEM, stream_handle())
     assert rc == -5
     assert lib.psgd_apply_noalloc(x.data_ptr(), 0, x.data_ptr(), 0, LR, MAX_AVG, MAX_ELEM, stream_handle()) == 0
+
+
+def test_noalloc_propagates_nan_like_the_reference(cuda):
+    """A NaN or an Inf in Pg reaches the parameter as NaN, as psgd_pro.py:371-381 does (Inf makes the RMS
+    infinite, the scale 0 and Inf * 0 = NaN); a clipped update must not hide a diverging run."""
+    pg = torch.randn(50_000, device=cuda) * 0.3
+    pg[123] = float("nan")
+    p0 = torch.randn(50_000, device=cuda) * 0.1
+    for bad in (float("nan"), float("inf")):
+        pg[123] = bad
+        r = reference_apply(p0, pg)
+        for fn in (apply_without_scratch, apply_with_caller_scratch):  # both entry points share the semantics
+            b = p0.clone()
+            fn(b, pg)
+            assert torch.equal(torch.isnan(b), torch.isnan(r)) and bool(torch.isnan(b[123])), (fn.__name__, bad)
+            fin = torch.isfinite(r)
+            assert rel(b[fin], r[fin]) < 1e-6, (fn.__name__, bad)
