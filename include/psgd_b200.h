@@ -105,6 +105,12 @@ int psgd_gemm_launch(const void* dev_table, const uint32_t* dev_tiles, int ntile
 /* Number of SMs the grouped launches use on the current device (grid size of the persistent kernels). */
 int psgd_num_sms(void);
 
+/* Layout check: writes sizeof of PsgdGemmSpec, PsgdPrepItem, PsgdNlbPrepItem, PsgdFactorItem, PsgdSkewItem,
+ * PsgdRotItem, PsgdTraceItem, PsgdApplyItem, PsgdBalanceFactor, PsgdBalanceParam, PsgdSymItem, PsgdNlbFinishItem
+ * (in this order, at most n of them) and returns how many structs there are (sizes may be NULL to ask). A binding
+ * compares them with its own struct definitions once, before its first launch. */
+int psgd_struct_sizes(long long* sizes, int n);
+
 /* ---------------------------------------------------------------------------------------------------------
  * Memory-bound step kernels. Each takes a device array of items (one per parameter or factor, encoded by the
  * caller), an optional device work list of (item, tile) pairs (uint32 pairs: item index, (ti << 16) | tj),
@@ -120,6 +126,8 @@ int psgd_num_sms(void);
 #define PSGD_HY_NOISE 7        /* nonzero: psgd_prep generates the damping noise itself (below) */
 #define PSGD_HY_NOISE_KEY0 8   /* the generator's key, two uint32 stored bit for bit in float slots */
 #define PSGD_HY_NOISE_KEY1 9
+#define PSGD_HY_EMA_PHASE 10   /* which staging pass of this step applies the momentum EMA (see PsgdPrepItem.m) */
+#define PSGD_HY_MOM_ALPHA 11   /* 1 - momentum factor of this step, as the caller rounds it to float */
 #define PSGD_HY_COUNT 12
 
 /* Gradient staging on 32 x 32 tiles of an n1 x n2 gradient G (fp32 or bf16, contiguous):
@@ -151,6 +159,12 @@ typedef struct PsgdPrepItem {
   float* part_row; float* part_col; float* part_tile;
   float eps;
   long long noise_base;  /* position of element 0 in the generated noise sequence (a multiple of 4) */
+  /* Momentum (psgd_pro.py:334-343), NULL for none: the buffer m (n1 x n2, g's dtype). When m is set, the staged
+   * source is the momentum instead of g: if mom_phase == hyper[PSGD_HY_EMA_PHASE] this pass first applies the EMA,
+   * m = rn(rn(beta m) + alpha g) with beta = hyper[PSGD_HY_MOM_BETA], alpha = hyper[PSGD_HY_MOM_ALPHA] (rn:
+   * rounding to g's dtype, as torch's in-place mul_ and add_ on that dtype), writes m back and stages it; otherwise it
+   * stages m as stored. */
+  void* m; int mom_phase;
 } PsgdPrepItem;
 int psgd_prep(const PsgdPrepItem* items, const uint32_t* work, int nwork, const float* hyper, int* dev_err,
               cudaStream_t stream);

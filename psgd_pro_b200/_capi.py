@@ -43,7 +43,7 @@ class PrepItem(ctypes.Structure):
     _fields_ = [("g", c_vp), ("g_bf16", c_int), ("mode", c_int), ("xi", c_vp), ("n1", c_int), ("n2", c_int),
                 ("p1", c_vp), ("p2", c_vp), ("out_hi", c_vp), ("out_lo", c_vp), ("ld_out", c_ll),
                 ("out_f32", c_vp), ("part_row", c_vp), ("part_col", c_vp), ("part_tile", c_vp), ("eps", c_float),
-                ("noise_base", c_ll)]
+                ("noise_base", c_ll), ("m", c_vp), ("mom_phase", c_int)]
 
 
 class NlbPrepItem(ctypes.Structure):
@@ -107,7 +107,7 @@ SKEW_TILE = 64
 FAC_SCRATCH = 32   # floats of scratch per diagonal factor item
 PSGD_FACTOR_DENSE, PSGD_FACTOR_RANK1, PSGD_FACTOR_DIAG, PSGD_FACTOR_SKEW = 0, 1, 2, 3
 HY_LR_PRECOND, HY_BETA_L, HY_DAMPING, HY_LR_PARAMS, HY_MAX_AVG, HY_MAX_ELEM, HY_MOM_BETA = range(7)
-HY_NOISE, HY_NOISE_KEY0, HY_NOISE_KEY1, HY_COUNT = 7, 8, 9, 12
+HY_NOISE, HY_NOISE_KEY0, HY_NOISE_KEY1, HY_EMA_PHASE, HY_MOM_ALPHA, HY_COUNT = 7, 8, 9, 10, 11, 12
 APPLY_CHUNK = 8192
 SYM_TILE = 64
 PSGD_SYM_SQUARE, PSGD_SYM_PACKED = 0, 1
@@ -134,7 +134,25 @@ SIGNATURES = [
     ("psgd_sym_expand", c_int, [c_vp, c_vp, c_int, c_vp, c_vp]),
     ("psgd_sym_reduce", c_int, [c_vp, c_int, c_int, c_vp, c_vp]),
     ("psgd_nlb_finish", c_int, [c_vp, c_int, c_vp, c_vp]),
+    ("psgd_struct_sizes", c_int, [c_vp, c_int]),
 ]
+
+# the structs in the order psgd_struct_sizes reports them
+STRUCTS = [GemmSpec, PrepItem, NlbPrepItem, FactorItem, SkewItem, RotItem, TraceItem, ApplyItem, BalanceFactor,
+           BalanceParam, SymItem, NlbFinishItem]
+
+
+def _check_layout(L):
+    """Refuses a library whose structs differ from these bindings (a stale build): a kernel would otherwise read
+    item arrays at the wrong stride."""
+    n = L.psgd_struct_sizes(None, 0)
+    sizes = (ctypes.c_longlong * n)()
+    L.psgd_struct_sizes(sizes, n)
+    mine = [ctypes.sizeof(c) for c in STRUCTS]
+    if n != len(mine) or list(sizes) != mine:
+        raise RuntimeError(f"psgd_pro_b200: {LIB_PATH} was built from another version of include/psgd_b200.h "
+                           f"(struct sizes {list(sizes)} against the bindings' {mine}); rebuild it with "
+                           "`python -m psgd_pro_b200.build`")
 
 _lib = None
 
@@ -150,6 +168,7 @@ def lib():
         for name, res, args in SIGNATURES:
             fn = getattr(L, name)
             fn.restype, fn.argtypes = res, args
+        _check_layout(L)
         _lib = L
     return _lib
 

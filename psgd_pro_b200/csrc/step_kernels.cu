@@ -19,6 +19,26 @@ PSGD_DEVI float load_g(const void* g, int bf16, long long idx) {
               : reinterpret_cast<const float*>(g)[idx];
 }
 
+PSGD_DEVI void store_g(void* g, int bf16, long long idx, float v) {
+  if (bf16) reinterpret_cast<__nv_bfloat16*>(g)[idx] = __float2bfloat16_rn(v);
+  else reinterpret_cast<float*>(g)[idx] = v;
+}
+
+// The momentum EMA of psgd_pro.py:340-341, m.mul_(beta).add_(g, alpha=1 - beta) on a tensor of g's dtype: each
+// in-place op rounds to that dtype (bf16: the product, then the sum).
+PSGD_DEVI float round_dt(float v, bool bf16) { return bf16 ? __bfloat162float(__float2bfloat16_rn(v)) : v; }
+PSGD_DEVI float ema_value(float m, float g, float beta, float alpha, bool bf16) {
+  return round_dt(fmaf(alpha, g, round_dt(m * beta, bf16)), bf16);
+}
+
+// The staged source value of element idx: g, or the momentum (after this pass's EMA when it applies it).
+PSGD_DEVI float load_src(const PsgdPrepItem& it, const void* src, bool ema, long long idx, float beta, float alpha) {
+  if (!ema) return load_g(src, it.g_bf16, idx);
+  const float v = ema_value(load_g(it.m, it.g_bf16, idx), load_g(it.g, it.g_bf16, idx), beta, alpha, it.g_bf16);
+  store_g(it.m, it.g_bf16, idx, v);
+  return v;
+}
+
 PSGD_DEVI void store_split(void* hi, void* lo, long long idx, float v) {
   __nv_bfloat16 h, l;
   split_bf16(v, h, l);
@@ -93,26 +113,34 @@ PSGD_DEVI void cp_async16_raw(void* dst, const void* src) {
                : "memory");
 }
 
-template <bool BF16>
-PSGD_DEVI void prep_rows_vec8(const PsgdPrepItem& it, long long r0, int rows, float damping, bool gen, uint32_t k0,
-                              uint32_t k1, uint4* stage) {
+// EMA: the item's momentum EMA runs in this pass (g is staged through shared memory, m is read into registers for
+// the whole batch before the conversions, and the new m is written back); otherwise `src` (g or m) is staged.
+template <bool BF16, bool EMA>
+PSGD_DEVI void prep_rows_vec8(const PsgdPrepItem& it, const void* gsrc, long long r0, int rows, float damping,
+                              bool gen, uint32_t k0, uint32_t k1, float mbeta, float malpha, uint4* stage) {
   constexpr int PV = BF16 ? PREP_VEC : PREP_VEC / 2, CH = BF16 ? 1 : 2;  // vectors per batch, chunks per vector
   const int nvr = it.n2 >> 3, nvec = rows * nvr, t = threadIdx.x;
   const float inv_nvr = 1.f / (float)nvr;
   for (int base = t; base < nvec; base += blockDim.x * PV) {
+    uint4 mv[EMA ? PV * CH : 1];
 #pragma unroll
     for (int s = 0; s < PV; ++s) {
       const int j = base + s * blockDim.x;
       if (j < nvec) {
         const int r = div_small(j, nvr, inv_nvr);
         const long long idx = (r0 + r) * it.n2 + (long long)(j - r * nvr) * 8;
-        const char* src = reinterpret_cast<const char*>(it.g) + idx * (BF16 ? 2 : 4);
+        const char* src = reinterpret_cast<const char*>(gsrc) + idx * (BF16 ? 2 : 4);
 #pragma unroll
         for (int c = 0; c < CH; ++c) cp_async16_raw(stage + (s * CH + c) * 256 + t, src + 16 * c);
+        if (EMA) {
+          const uint4* mp = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(it.m) + idx * (BF16 ? 2 : 4));
+#pragma unroll
+          for (int c = 0; c < CH; ++c) mv[(s * CH + c) % (EMA ? PV * CH : 1)] = mp[c];
+        }
       }
     }
     asm volatile("cp.async.wait_all;\n" ::: "memory");
-#pragma unroll 1
+#pragma unroll(EMA ? PV : 1)
     for (int s = 0; s < PV; ++s) {
       const int j = base + s * blockDim.x;
       if (j >= nvec) break;
@@ -129,6 +157,33 @@ PSGD_DEVI void prep_rows_vec8(const PsgdPrepItem& it, long long r0, int rows, fl
         const float4 b = reinterpret_cast<const float4*>(stage)[(2 * s + 1) * 256 + t];
         x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
         x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+      }
+      if (EMA) {  // x holds g: m = rn(rn(beta m) + alpha g), written back, then staged
+        uint4 mo[CH];
+        if (BF16) {
+          const uint4 v = mv[(s * CH) % (EMA ? PV * CH : 1)];
+          const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&v);
+          __align__(16) __nv_bfloat16 o[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            o[i] = __float2bfloat16_rn(fmaf(malpha, x[i], round_dt(__bfloat162float(h[i]) * mbeta, true)));
+            x[i] = __bfloat162float(o[i]);
+          }
+          mo[0] = *reinterpret_cast<const uint4*>(o);
+        } else {
+#pragma unroll
+          for (int c = 0; c < CH; ++c) {
+            const uint4 v = mv[(s * CH + c) % (EMA ? PV * CH : 1)];
+            const float mm[4] = {__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w)};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) x[4 * c + i] = fmaf(malpha, x[4 * c + i], mm[i] * mbeta);
+            mo[c] = make_uint4(__float_as_uint(x[4 * c]), __float_as_uint(x[4 * c + 1]), __float_as_uint(x[4 * c + 2]),
+                               __float_as_uint(x[4 * c + 3]));
+          }
+        }
+        uint4* mp = reinterpret_cast<uint4*>(reinterpret_cast<char*>(it.m) + idx * (BF16 ? 2 : 4));
+#pragma unroll
+        for (int c = 0; c < CH; ++c) mp[c] = mo[c];
       }
       if (it.xi) {
 #pragma unroll
@@ -170,26 +225,39 @@ __global__ void __launch_bounds__(256) prep_kernel(const PsgdPrepItem* __restric
   const float damping = hyper[PSGD_HY_DAMPING];
   const bool gen = hyper[PSGD_HY_NOISE] != 0.f;  // noise from the counter-based generator instead of xi
   const uint32_t k0 = __float_as_uint(hyper[PSGD_HY_NOISE_KEY0]), k1 = __float_as_uint(hyper[PSGD_HY_NOISE_KEY1]);
+  const float mbeta = hyper[PSGD_HY_MOM_BETA], malpha = hyper[PSGD_HY_MOM_ALPHA];
+  const int ema_phase = (int)hyper[PSGD_HY_EMA_PHASE];
   for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
     const PsgdPrepItem& it = items[work[2 * w]];
+    // the staged source: g, or the momentum (this pass applies its EMA when the item's phase is this step's)
+    const bool ema = it.m != nullptr && it.mom_phase == ema_phase;
+    const void* src = (it.m != nullptr && !ema) ? it.m : it.g;
     if (it.mode == PSGD_PREP_NORMAL) {  // rows PREP_ROWS * wv .. : 4-element vectors along each row
       const long long r0 = (long long)work[2 * w + 1] * PREP_ROWS;
       const int rows = (int)min((long long)PREP_ROWS, it.n1 - r0);
-      const bool vec = (it.n2 % 8) == 0 && (reinterpret_cast<uintptr_t>(it.g) & 15) == 0 &&
+      const bool vec = (it.n2 % 8) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0 &&
+                       (!ema || (reinterpret_cast<uintptr_t>(it.m) & 15) == 0) &&
                        (it.xi == nullptr || (reinterpret_cast<uintptr_t>(it.xi) & 15) == 0) &&
                        (it.noise_base & 3) == 0 && (it.ld_out % 8) == 0 &&
                        (reinterpret_cast<uintptr_t>(it.out_hi) & 15) == 0 &&
                        (reinterpret_cast<uintptr_t>(it.out_lo) & 15) == 0;
       if (vec) {
-        if (it.g_bf16)
-          prep_rows_vec8<true>(it, r0, rows, damping, gen, k0, k1, prep_stage);
-        else
-          prep_rows_vec8<false>(it, r0, rows, damping, gen, k0, k1, prep_stage);
+        if (ema) {
+          if (it.g_bf16)
+            prep_rows_vec8<true, true>(it, src, r0, rows, damping, gen, k0, k1, mbeta, malpha, prep_stage);
+          else
+            prep_rows_vec8<false, true>(it, src, r0, rows, damping, gen, k0, k1, mbeta, malpha, prep_stage);
+        } else {
+          if (it.g_bf16)
+            prep_rows_vec8<true, false>(it, src, r0, rows, damping, gen, k0, k1, mbeta, malpha, prep_stage);
+          else
+            prep_rows_vec8<false, false>(it, src, r0, rows, damping, gen, k0, k1, mbeta, malpha, prep_stage);
+        }
       } else {
         for (int k = threadIdx.x; k < rows * it.n2; k += blockDim.x) {
           const long long row = r0 + k / it.n2, col = k % it.n2;
           const long long idx = row * it.n2 + col;
-          float x = load_g(it.g, it.g_bf16, idx);
+          float x = load_src(it, src, ema, idx, mbeta, malpha);
           if (it.xi) x += (damping + it.eps * fabsf(x)) * (gen ? normal1(it.noise_base + idx, k0, k1) : it.xi[idx]);
           store_split(it.out_hi, it.out_lo, row * it.ld_out + col, x);
         }
@@ -206,7 +274,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const PsgdPrepItem* __restric
       float x = 0.f;
       if (i < it.n1 && j < it.n2) {
         const long long idx = (long long)i * it.n2 + j;
-        x = load_g(it.g, it.g_bf16, idx);
+        x = load_src(it, src, ema, idx, mbeta, malpha);
         if (it.xi) x += (damping + it.eps * fabsf(x)) * (gen ? normal1(it.noise_base + idx, k0, k1) : it.xi[idx]);
       }
       vals[u] = x;

@@ -5,7 +5,7 @@ import ctypes
 import torch
 
 from . import _capi
-from ._capi import GemmSpec, PSGD_GEMM_PLAIN, PSGD_GEMM_SYRK, check
+from ._capi import GemmSpec, PSGD_GEMM_PLAIN, PSGD_GEMM_SYRK, PSGD_GEMM_TRMM, check
 
 BF16 = torch.bfloat16
 

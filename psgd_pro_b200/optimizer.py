@@ -30,7 +30,8 @@ from . import _capi
 from . import kernels as K
 from ._capi import (PSGD_FACTOR_DENSE, PSGD_FACTOR_DIAG, PSGD_FACTOR_RANK1, PSGD_FACTOR_SKEW, PSGD_PREP_DIRECT,
                     PSGD_PREP_NORMAL, PSGD_PREP_TRANS, HY_COUNT, HY_LR_PRECOND, HY_BETA_L, HY_DAMPING, HY_LR_PARAMS,
-                    HY_MAX_AVG, HY_MAX_ELEM, HY_MOM_BETA, HY_NOISE, HY_NOISE_KEY0, HY_NOISE_KEY1, APPLY_CHUNK, check)
+                    HY_MAX_AVG, HY_MAX_ELEM, HY_MOM_BETA, HY_MOM_ALPHA, HY_EMA_PHASE, HY_NOISE, HY_NOISE_KEY0,
+                    HY_NOISE_KEY1, APPLY_CHUNK, check)
 
 K_SUB = 32  # subspace dimension of the norm lower bounds (psgd_pro.py:19, psgd_pro_fast.py:29)
 TT = 32     # tile edge of the element-wise kernels
@@ -202,6 +203,7 @@ class _Plan:
             f.v_skh = self.vbuf[off + K_SUB * f.n:off + 2 * K_SUB * f.n].view(K_SUB, f.n)
             off += 2 * K_SUB * f.n
         self.grad_ptrs = None
+        self.mom_key, self.ms_ptrs = None, None
 
     def new_factor(self, kind, n, scale, numel, rank1=False):
         f = _Factor(kind, n, scale, numel, len(self.factors), self, rank1)
@@ -224,12 +226,16 @@ class _Plan:
     def s(self, f, slot):
         return self.scal[f.fidx, slot:slot + 1]
 
-    def build(self, src_update, src_apply, grad_eps):
-        """Encodes every phase. src_update / src_apply: the tensors whittened / preconditioned (gradients or
-        momentum buffers), in parameter order; their data pointers are baked into the prep items."""
+    def build(self, grads, ms, whiten_grad, grad_eps):
+        """Encodes every phase. grads: the gradients in parameter order (their data pointers are baked into the
+        staging items; update_grad_ptrs re-points them); ms: the momentum buffers or None. The staging passes
+        take the momentum as their source where the reference does (psgd_pro.py:350-361: the update whitens g or m,
+        the preconditioner is applied to m when there is momentum) and apply its EMA in the first pass of the step
+        that reads it (hyper[HY_EMA_PHASE]: 1 when the update runs first on m, else 0)."""
         dev, split = self.device, self.split
         P = self.params
-        self.grad_ptrs = (tuple(t.data_ptr() for t in src_update), tuple(t.data_ptr() for t in src_apply))
+        self.grad_ptrs = tuple(t.data_ptr() for t in grads)
+        self.mom_key = (ms is not None, bool(whiten_grad))
         self._ptr_items = {}
         # U0 / A0: gradient staging
         self.prep_u, self.prep_a = [], []
@@ -237,9 +243,11 @@ class _Plan:
         self.t1 = {}
         for k, p in enumerate(P):
             kind = p.kind
-            for phase, src, items, pairs in (("u", src_update[k], self.prep_u, pu), ("a", src_apply[k], self.prep_a, pa)):
+            for phase, src, items, pairs in (("u", grads[k], self.prep_u, pu), ("a", grads[k], self.prep_a, pa)):
                 it = _capi.PrepItem()
                 it.g, it.g_bf16 = src.data_ptr(), int(src.dtype == torch.bfloat16)
+                if ms is not None and (phase == "a" or not whiten_grad):
+                    it.m, it.mom_phase = ms[k].data_ptr(), (1 if phase == "u" else 0)
                 it.xi = p.xi.data_ptr() if phase == "u" else None
                 it.noise_base = p.xi_off
                 it.n1, it.n2, it.eps = p.n1, p.n2, grad_eps[k]
@@ -509,18 +517,18 @@ class _Plan:
             groups.append(self.group(specs))
         return groups
 
-    def update_grad_ptrs(self, src_update, src_apply):
+    def update_grad_ptrs(self, grads):
         """Re-point the staging items at this step's gradient tensors (only when their addresses changed). The item
         arrays of each address set are built on the device once; switching sets is a device-to-device copy into
         the live arrays (stream-ordered, no host wait, captured graphs stay valid)."""
-        ptrs = (tuple(t.data_ptr() for t in src_update), tuple(t.data_ptr() for t in src_apply))
+        ptrs = tuple(t.data_ptr() for t in grads)
         if ptrs == self.grad_ptrs:
             return
         cached = self._ptr_items.get(ptrs)
         if cached is None:
             cached = []
-            for items, src in ((self.prep_u, src_update), (self.prep_a, src_apply)):
-                for it, t in zip(items, src):
+            for items in (self.prep_u, self.prep_a):
+                for it, t in zip(items, grads):
                     it.g, it.g_bf16 = t.data_ptr(), int(t.dtype == torch.bfloat16)
                 cached.append(_upload(_capi.PrepItem, items, self.device))
             if len(self._ptr_items) >= 8:  # a handful of gradient buffers in rotation at most
@@ -742,21 +750,26 @@ class KronWhiten:
                 else:
                     f.p.copy_(f.q * f.q)
             if st.get("m") is not None:
+                m = torch.as_tensor(st["m"]).to(self._device)
                 if self._ms is None:
-                    self._ms = [torch.zeros_like(q.squeeze()) for q in self._params_with_grad]
-                self._ms[k].copy_(st["m"])
+                    self._ms = [torch.zeros(q.squeeze().shape, dtype=m.dtype, device=self._device)
+                                for q in self._params_with_grad]
+                if self._ms[k].dtype != m.dtype or self._ms[k].shape != m.shape:
+                    self._ms[k] = torch.zeros(m.shape, dtype=m.dtype, device=self._device)
+                self._ms[k].copy_(m)
         self._counter_m = sd.get("counter_m", 0)
         self._graphs = {}
 
     # ---- the step ------------------------------------------------------------------------------------------
-    def _set_hyper(self, beta_m=0.0, noise=None):
+    def _set_hyper(self, beta_m=0.0, noise=None, ema_phase=0):
         """Device hyper-parameter vector. noise: None (the damping noise is read from the draws buffer) or the
-        (key0, key1) of the in-kernel generator."""
+        (key0, key1) of the in-kernel generator; ema_phase: the staging pass that applies the momentum EMA."""
         h = [0.0] * HY_COUNT
         h[HY_LR_PRECOND], h[HY_BETA_L], h[HY_DAMPING] = self.lr_preconditioner, self.betaL, self.damping
         h[HY_LR_PARAMS] = self.lr_params
         h[HY_MAX_AVG], h[HY_MAX_ELEM] = self.grad_clip_max_amps
-        h[HY_MOM_BETA] = beta_m
+        h[HY_MOM_BETA], h[HY_MOM_ALPHA] = beta_m, 1 - beta_m  # psgd_pro.py:341: mul_(beta).add_(g, alpha=1 - beta)
+        h[HY_EMA_PHASE] = float(ema_phase)
         bits = [struct.unpack("<i", struct.pack("<f", float(x)))[0] for x in h]
         if noise is not None:
             bits[HY_NOISE] = struct.unpack("<i", struct.pack("<f", 1.0))[0]
@@ -813,26 +826,28 @@ class KronWhiten:
             self._build(init_scale_from_grads(grads, self.damping))
         plan = self._plan
         beta = 0.0
-        if self.momentum > 0:  # psgd_pro.py:334-343
+        if self.momentum > 0:  # psgd_pro.py:334-343; the EMA itself runs in the staging kernel
             beta = min(self._counter_m / (1 + self._counter_m), self.momentum)
-            self._counter_m += 1
-            if self._ms is None:
+            if self._ms is None or any(m.dtype != g.dtype or m.shape != g.shape for m, g in zip(self._ms, grads)):
                 self._ms = [torch.zeros_like(g) for g in grads]
-            torch._foreach_mul_(self._ms, beta)
-            torch._foreach_add_(self._ms, grads, alpha=1 - beta)
+            elif self._counter_m == 0:  # momentum (re)started: the reference starts from zeros
+                for m in self._ms:
+                    m.zero_()
+            self._counter_m += 1
         else:
             self._ms, self._counter_m = None, 0
-        src_u = grads if self._whiten_grad else self._ms
-        src_a = self._ms if self.momentum > 0 else grads
-        if plan.grad_ptrs is None:
-            eps = [torch.finfo(g.dtype).eps for g in src_u]  # psgd_pro.py:122
-            plan.build(src_u, src_a, eps)
+        ms = self._ms if self.momentum > 0 else None
+        key = (ms is not None, bool(self._whiten_grad))
+        stale = ms is not None and plan.ms_ptrs != [m.data_ptr() for m in ms]
+        if plan.grad_ptrs is None or plan.mom_key != key or stale:
+            eps = [torch.finfo(g.dtype).eps for g in grads]  # psgd_pro.py:122
+            plan.build(grads, ms, self._whiten_grad, eps)
+            plan.ms_ptrs = [m.data_ptr() for m in ms] if ms is not None else None
             self._graphs = {}
-        elif (tuple(t.data_ptr() for t in src_u), tuple(t.data_ptr() for t in src_a)) != plan.grad_ptrs:
-            plan.update_grad_ptrs(src_u, src_a)
+        elif tuple(t.data_ptr() for t in grads) != plan.grad_ptrs:
+            plan.update_grad_ptrs(grads)
         if draws is None and self._noise_key is None:
             self._noise_key = int(torch.randint(0, 2 ** 31, (1,)).item())
-        self._set_hyper(beta, noise=(self._noise_key, self._steps) if draws is None else None)
         if draws is None:
             update = bool(torch.rand([]) < self.preconditioner_update_probability)
             coins = (torch.rand(len(plan.params)) < 0.01).tolist() if update else []
@@ -843,6 +858,10 @@ class KronWhiten:
             use_graph = False
             if update:
                 self._load_draws(draws["normals"])
+        # the momentum EMA runs in the first staging pass of this step that reads the momentum
+        ema_phase = 1 if (ms is not None and not self._whiten_grad and update and self.update_preconditioner_first) \
+            else 0
+        self._set_hyper(beta, noise=(self._noise_key, self._steps) if draws is None else None, ema_phase=ema_phase)
 
         trace = self.trace
         if trace is not None:

@@ -111,3 +111,43 @@ def test_state_dict_roundtrip(cuda):
             assert rel(qc.cpu().numpy(), qa.cpu().numpy()) < 1e-5
     for x, y in zip(pa, pc):
         assert rel(y.detach().cpu().numpy(), x.detach().cpu().numpy()) < 1e-6
+
+
+@pytest.mark.parametrize("whiten_grad,update_first,gdt", [(False, True, torch.float32), (False, False, torch.float32),
+                                                          (True, True, torch.bfloat16), (False, True, torch.bfloat16)])
+def test_momentum_in_the_staging_kernel(cuda, whiten_grad, update_first, gdt):
+    """The momentum EMA (psgd_pro.py:334-343) runs inside the staging kernel, in whichever staging pass of the step
+    reads the momentum first; with update probability 1/2 the preconditioner update is skipped on some steps, so
+    the EMA moves between the update's pass and the apply's pass. Compared with the oracle on the same draws; with
+    bf16 gradients the momentum is a bf16 tensor as in the reference (rounded at each in-place op), so the bar is
+    the bf16 one."""
+    rng = np.random.default_rng(21)
+    shapes = [(48, 80), (65,), (100, 20), (30, 30)]
+    kw = dict(momentum=0.9, whiten_grad=whiten_grad, update_preconditioner_first=update_first,
+              preconditioner_update_probability=0.5, preconditioner_max_skew=float("inf"),
+              preconditioner_init_scale=0.7, lr_params=1e-2)
+    p0 = [rng.standard_normal(s, dtype=np.float32) for s in shapes]
+    ora = O.KronWhitenOracle(p0, dtype=np.float64, **kw)
+    params = [torch.nn.Parameter(torch.from_numpy(p.copy()).to(cuda)) for p in p0]
+    opt = KronWhiten(params, precision="fp32", **kw)
+    fired = set()
+    for step in range(6):
+        G = [(rng.standard_normal(s, dtype=np.float32) * np.float32(0.01)) for s in shapes]
+        Gd = [torch.from_numpy(g).to(cuda).to(gdt) for g in G]
+        G = [gd.float().cpu().numpy() for gd in Gd]  # the values the device sees
+        d = ora.make_draws(rng, G)
+        fired.add(d["update"] < 0.5)
+        pre = ora.step(G, d)
+        opt.step_math(Gd, draws=d)
+    torch.cuda.synchronize()
+    opt.check_errors()
+    assert fired == {True, False}  # both orders of the EMA occurred
+    tol = TOL["fp32"] if gdt == torch.float32 else TOL["bf16"]
+    st = opt.state_dict()
+    for k, ((Qo, _), s) in enumerate(zip(ora.QL, st["state"])):
+        for qo, qg in zip(Qo, s["Q"]):
+            assert rel(qg.cpu().numpy(), qo) < tol
+        assert rel(s["m"].float().cpu().numpy(), ora.ms[k]) < tol
+        pg = opt._plan.params[k].pg32.cpu().numpy().reshape(np.shape(pre[k]))
+        assert rel(pg, pre[k]) < tol
+    assert st["counter_m"] == 6
