@@ -92,7 +92,7 @@ int psgd_gemm(const PsgdGemmSpec* spec, int split, int* dev_err, cudaStream_t st
  * a CUDA graph). The tile list (uint32 pairs; psgd_gemm_count_tiles gives its length, *ntiles the entries used)
  * starts with a header that splits the tiles into one segment per SM: tiles are taken in the order the specs are
  * given (callers put the costliest problems first) and each goes to the SM with the least estimated work so far.
- * Encoding also reports the group's kernel (*kind: the epilogue kind 0..4, plus 8 for CTA pairs or 16 for the
+ * Encoding also reports the group's kernel (*kind: the epilogue kind 0..5, plus 8 for CTA pairs or 16 for the
  * narrow ring), which the launch takes back: interior tiles of the problems of that epilogue kind run a specialised
  * epilogue, all other tiles the general one. */
 size_t psgd_gemm_table_bytes(int nspecs);

@@ -116,7 +116,10 @@ PSGD_DEVI void st4b(__nv_bfloat16* hi, __nv_bfloat16* lo, const float* x, int n,
   }
 }
 
-template <int BNMAX>
+// PACKED: the packed-triangle store is compiled in (only the kernels that can meet a problem with out_packed: the
+// general and packed-SYRK kinds; encoding keeps such problems out of groups of other kinds, whose register budget
+// it would otherwise take).
+template <int BNMAX, bool PACKED>
 __device__ __forceinline__ void epilogue_tile(const GemmDesc& d, int tm, int tn, uint32_t tacc, int q, int lane, float* red,
                               float* cs, float* misc, float* stage) {
   // Every descriptor field the loops use is copied into a register first: the staging stores go through
@@ -315,7 +318,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmDesc& d, int tm, int tn,
               for (int i = 0; i < 4; ++i)
                 if (i >= first && i < ncv) dsum += x[i] * dd[i];
             }
-            if (s_out_packed) {
+            if (PACKED && s_out_packed) {
               const long long pb = packed_off(gr, gcb, s_N);
 #pragma unroll
               for (int i = 0; i < 4; ++i)
@@ -444,12 +447,13 @@ __device__ __forceinline__ void epilogue_tile(const GemmDesc& d, int tm, int tn,
 // kind. The column pass is epilogue_tile's; the transposed pass keeps one accumulator row per lane (the TMEM
 // layout) so each warp store writes 32 consecutive elements of a transposed row, and reads no shared memory in
 // SYRK mode. SYRK tiles that meet the diagonal mask only the one 32 x 32 chunk per warp that the diagonal crosses.
-enum : int { EPI_GENERIC = 0, EPI_AUX = 1, EPI_NLB = 2, EPI_PLAIN = 3, EPI_SYRK = 4 };
+// EPI_SYRKP: SYRK whose only output is the packed upper triangle (no mirror, no reductions).
+enum : int { EPI_GENERIC = 0, EPI_AUX = 1, EPI_NLB = 2, EPI_PLAIN = 3, EPI_SYRK = 4, EPI_SYRKP = 5 };
 
 template <int KIND, int BNMAX, bool DG>
 __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn, uint32_t tacc, int q, int lane, float* red,
                               float* cs, float* misc, float* stage) {
-  static_assert(!DG || KIND == EPI_SYRK, "diagonal tiles exist in SYRK mode only");
+  static_assert(!DG || KIND == EPI_SYRK || KIND == EPI_SYRKP, "diagonal tiles exist in SYRK mode only");
   const PsgdGemmSpec& sd = d.s;
   const long long s_M = sd.M, s_N = sd.N;
   const int bn = sd.bn;
@@ -577,6 +581,12 @@ __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn,
         if (s_out_f32)
           *reinterpret_cast<float4*>(s_out_f32 + row * s_ld_f32 + colb) = make_float4(x[0], x[1], x[2], x[3]);
         if (out_hi) st4b(out_hi + row * s_ld_b + colb, out_lo ? out_lo + row * s_ld_b + colb : nullptr, x, 4, true);
+      } else if (KIND == EPI_SYRKP) {  // packed upper triangle only: four consecutive values of row `row`
+        float* pp = s_out_packed + packed_off(row, colb, s_N);  // (unaligned offsets: scalar stores)
+        const int first = MASK ? (int)max(0LL, min(4LL, row - colb)) : 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (i >= first) pp[i] = x[i];
       } else if (!MASK) {  // EPI_SYRK above the diagonal: every element is direct and has a mirror
         float rp = 0.f;
 #pragma unroll
@@ -591,13 +601,6 @@ __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn,
           *reinterpret_cast<float4*>(s_out_f32 + row * s_ld_f32 + colb) = make_float4(x[0], x[1], x[2], x[3]);
         if (out_hi) st4b(out_hi + row * s_ld_b + colb, out_lo ? out_lo + row * s_ld_b + colb : nullptr, x, 4, true);
         if (s_dot) dsum += x[0] * pv[it].x + x[1] * pv[it].y + x[2] * pv[it].z + x[3] * pv[it].w;
-        if (s_out_packed) {  // four consecutive values of row `row` (no vector store: the offsets are unaligned)
-          float* pp = s_out_packed + packed_off(row, colb, s_N);
-          pp[0] = x[0];
-          pp[1] = x[1];
-          pp[2] = x[2];
-          pp[3] = x[3];
-        }
       } else {  // EPI_SYRK on the diagonal: element i is direct when colb + i >= row, mirrored when >
         const int first = (int)max(-1LL, min(4LL, row - colb));
         const float dd[4] = {pv[it].x, pv[it].y, pv[it].z, pv[it].w};
@@ -611,7 +614,6 @@ __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn,
           csq[i] += (i > first) ? x2 : 0.f;
           if (i == first && s_diag_out) s_diag_out[row] = x[i];
           if (direct) {
-            if (s_out_packed) s_out_packed[packed_off(row, colb + i, s_N)] = x[i];
             if (s_out_f32) s_out_f32[row * s_ld_f32 + colb + i] = x[i];
             if (out_hi) {
               __nv_bfloat16 h, l;
@@ -951,13 +953,13 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
       // the launch's kind (template) picks the one fast path compiled into this kernel; problems of another
       // kind, edge tiles and SYRK tiles on the diagonal take the generic epilogue
       const bool fast = KIND != EPI_GENERIC && d.fast == KIND && interior;
-      if constexpr (KIND == EPI_SYRK) {
+      if constexpr (KIND == EPI_SYRK || KIND == EPI_SYRKP) {
         if (fast && n0 >= m0 + BM) epilogue_fast<KIND, BNMAX, false>(d, tm, tn, tacc, q, lane, red, cs, misc, stg);
         else if (fast) epilogue_fast<KIND, BNMAX, true>(d, tm, tn, tacc, q, lane, red, cs, misc, stg);
-        else epilogue_tile<BNMAX>(d, tm, tn, tacc, q, lane, red, cs, misc, stg);
+        else epilogue_tile<BNMAX, KIND == EPI_GENERIC || KIND == EPI_SYRKP>(d, tm, tn, tacc, q, lane, red, cs, misc, stg);
       } else {
         if (fast) epilogue_fast<KIND, BNMAX, false>(d, tm, tn, tacc, q, lane, red, cs, misc, stg);
-        else epilogue_tile<BNMAX>(d, tm, tn, tacc, q, lane, red, cs, misc, stg);
+        else epilogue_tile<BNMAX, KIND == EPI_GENERIC || KIND == EPI_SYRKP>(d, tm, tn, tacc, q, lane, red, cs, misc, stg);
       }
       tc_fence_before();
       __syncwarp();
@@ -1176,13 +1178,13 @@ __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ desc
       if (m0 < d.s.M) {
         const bool interior = m0 + BM <= d.s.M && n0 + d.s.bn <= d.s.N;
         const bool fast = KIND != EPI_GENERIC && d.fast == KIND && interior;
-        if constexpr (KIND == EPI_SYRK) {
+        if constexpr (KIND == EPI_SYRK || KIND == EPI_SYRKP) {
           if (fast && n0 >= m0 + BM) epilogue_fast<KIND, BNMAX, false>(d, tm128, tn, tacc, q, lane, red, cs, misc, stg);
           else if (fast) epilogue_fast<KIND, BNMAX, true>(d, tm128, tn, tacc, q, lane, red, cs, misc, stg);
-          else epilogue_tile<BNMAX>(d, tm128, tn, tacc, q, lane, red, cs, misc, stg);
+          else epilogue_tile<BNMAX, KIND == EPI_GENERIC || KIND == EPI_SYRKP>(d, tm128, tn, tacc, q, lane, red, cs, misc, stg);
         } else {
           if (fast) epilogue_fast<KIND, BNMAX, false>(d, tm128, tn, tacc, q, lane, red, cs, misc, stg);
-          else epilogue_tile<BNMAX>(d, tm128, tn, tacc, q, lane, red, cs, misc, stg);
+          else epilogue_tile<BNMAX, KIND == EPI_GENERIC || KIND == EPI_SYRKP>(d, tm128, tn, tacc, q, lane, red, cs, misc, stg);
         }
       }
       tc_fence_before();
@@ -1275,7 +1277,12 @@ static int fast_kind(const PsgdGemmSpec& s) {
   // the fast epilogue walks whole 32-column chunks: narrower tiles (bn = 16) would run past the output
   if (s.bn % 32 != 0) return EPI_GENERIC;
   if (!(f32_ok && b_ok && t_ok && aux_ok && dot_ok) || s.col_scale) return EPI_GENERIC;
-  if (s.mode == PSGD_GEMM_SYRK) return s.row_scale || s.aux || s.cs_mode || s.out_hi_t ? EPI_GENERIC : EPI_SYRK;
+  if (s.mode == PSGD_GEMM_SYRK) {
+    if (s.row_scale || s.aux || s.cs_mode || s.out_hi_t) return EPI_GENERIC;
+    if (s.out_packed)  // the packed triangle alone has its own fast path; with other outputs the general one
+      return (s.out_f32 || s.out_hi || s.dot_aux || s.diag_out || s.part_row || s.part_tile) ? EPI_GENERIC : EPI_SYRKP;
+    return EPI_SYRK;
+  }
   if (s.aux)
     return (s.out_f32 && s.out_hi_t && !s.out_hi && !s.row_scale && !s.cs_mode && !s.part_tile && !s.part_col &&
             !s.part_row && !s.dot_aux) ? EPI_AUX : EPI_GENERIC;
@@ -1322,13 +1329,25 @@ static int spec_tiles(const PsgdGemmSpec& s, int bm = BM) {
 // same time (neighbours in this order) share a few B panels and a band of A panels that stay resident in L2.
 constexpr int RASTER_W = 8;
 
+// Width of the column blocks: RASTER_W, or PSGD_GEMM_RASTER from the environment (a positive count of tile columns;
+// 0 walks whole rows), read at encoding time.
+static int raster_width() {
+  const char* env = getenv("PSGD_GEMM_RASTER");
+  if (env && env[0]) {
+    const int w = atoi(env);
+    return w > 0 ? w : 1 << 30;
+  }
+  return RASTER_W;
+}
+
 static void append_tiles(const PsgdGemmSpec& s, uint32_t p, uint32_t* out, int& k, int bm = BM) {
   const int tmn = (s.M + bm - 1) / bm, tnn = (s.N + s.bn - 1) / s.bn;
   const bool syrk = s.mode == PSGD_GEMM_SYRK;
-  for (int c0 = 0; c0 < tnn; c0 += RASTER_W)
+  const int rw = raster_width();
+  for (int c0 = 0; c0 < tnn; c0 += rw)
     for (int tm = 0; tm < tmn; ++tm) {
       const int lo = syrk ? max(c0, tm * bm / s.bn) : c0;
-      for (int tn = lo; tn < min(c0 + RASTER_W, tnn); ++tn) {
+      for (int tn = lo; tn < min(c0 + rw, tnn); ++tn) {
         out[2 * k] = p;
         out[2 * k + 1] = ((uint32_t)tm << 16) | (uint32_t)tn;
         ++k;
@@ -1430,6 +1449,7 @@ static int launch_pair_kind(const GemmDesc* d, const uint32_t* tiles, int kind, 
     case EPI_NLB: return launch_pair<EPI_NLB>(d, tiles, err, st);
     case EPI_PLAIN: return launch_pair<EPI_PLAIN>(d, tiles, err, st);
     case EPI_SYRK: return launch_pair<EPI_SYRK>(d, tiles, err, st);
+    case EPI_SYRKP: return launch_pair<EPI_SYRKP>(d, tiles, err, st);
     default: return launch_pair<EPI_GENERIC>(d, tiles, err, st);
   }
 }
@@ -1471,6 +1491,7 @@ static int launch_group_kind(const GemmDesc* d, const uint32_t* tiles, int ntile
     case EPI_NLB: return launch_group<SPLIT, BNMAX, STAGES, EPI_NLB>(d, tiles, ntiles, err, st);
     case EPI_PLAIN: return launch_group<SPLIT, BNMAX, STAGES, EPI_PLAIN>(d, tiles, ntiles, err, st);
     case EPI_SYRK: return launch_group<SPLIT, BNMAX, STAGES, EPI_SYRK>(d, tiles, ntiles, err, st);
+    case EPI_SYRKP: return launch_group<SPLIT, BNMAX, STAGES, EPI_SYRKP>(d, tiles, ntiles, err, st);
     default: return launch_group<SPLIT, BNMAX, STAGES, EPI_GENERIC>(d, tiles, ntiles, err, st);
   }
 }
@@ -1482,6 +1503,7 @@ static int launch_single_kind(const GemmDesc& d, int ntiles, int* err, cudaStrea
     case EPI_NLB: return launch_single<SPLIT, BNMAX, STAGES, EPI_NLB>(d, nullptr, ntiles, err, st);
     case EPI_PLAIN: return launch_single<SPLIT, BNMAX, STAGES, EPI_PLAIN>(d, nullptr, ntiles, err, st);
     case EPI_SYRK: return launch_single<SPLIT, BNMAX, STAGES, EPI_SYRK>(d, nullptr, ntiles, err, st);
+    case EPI_SYRKP: return launch_single<SPLIT, BNMAX, STAGES, EPI_SYRKP>(d, nullptr, ntiles, err, st);
     default: return launch_single<SPLIT, BNMAX, STAGES, EPI_GENERIC>(d, nullptr, ntiles, err, st);
   }
 }
@@ -1536,11 +1558,18 @@ extern "C" int psgd_gemm_encode(const PsgdGemmSpec* specs, int nspecs, void* hos
     if (rc) return rc;
   }
   // the group's epilogue kind: the fast kind covering the most tiles (its problems take the fast path)
-  long long w[5] = {0, 0, 0, 0, 0};
+  long long w[6] = {0, 0, 0, 0, 0, 0};
   for (int i = 0; i < nspecs; ++i) w[descs[i].fast] += spec_tiles(specs[i], bm);
   int best = EPI_GENERIC;
-  for (int t = 1; t < 5; ++t)
+  for (int t = 1; t < 6; ++t)
     if (w[t] > w[best] || (best == EPI_GENERIC && w[t] > 0)) best = t;
+  // problems with a packed output only run in kernels that compile the packed store in
+  bool any_packed = false, all_syrkp = true;
+  for (int i = 0; i < nspecs; ++i) {
+    any_packed = any_packed || specs[i].out_packed != nullptr;
+    all_syrkp = all_syrkp && descs[i].fast == EPI_SYRKP;
+  }
+  if (any_packed) best = all_syrkp ? EPI_SYRKP : EPI_GENERIC;
   // Narrow groups (the N = 32 norm-bound products, the rank-one products) are memory-bound streams of their A
   // operand: they run on a configuration for tiles up to 64 wide whose stages hold four 64-deep K blocks.
   bool narrow = !pair;
@@ -1591,7 +1620,7 @@ extern "C" int psgd_gemm_encode(const PsgdGemmSpec* specs, int nspecs, void* hos
 
 extern "C" int psgd_gemm_launch(const void* dev_table, const uint32_t* dev_tiles, int ntiles, int split, int kind,
                                 int* dev_err, cudaStream_t stream) {
-  if (!dev_table || !dev_tiles || ntiles < 0 || !dev_err || kind < 0 || (kind & 7) > 4 ||
+  if (!dev_table || !dev_tiles || ntiles < 0 || !dev_err || kind < 0 || (kind & 7) > EPI_SYRKP ||
       (kind & ~(7 | KIND_PAIR | KIND_NARROW)) != 0 || ((kind & KIND_PAIR) && (kind & KIND_NARROW)))
     return PSGD_EINVAL;
   if (ntiles == 0) return PSGD_OK;
@@ -1609,6 +1638,7 @@ extern "C" int psgd_gemm(const PsgdGemmSpec* spec, int split, int* dev_err, cuda
   GemmDesc desc;
   int rc = fill_desc(&desc, *spec, split);
   if (rc) return rc;
+  if (spec->out_packed && desc.fast != EPI_SYRKP) desc.fast = EPI_GENERIC;
   const int nt = spec_tiles(*spec);
   if (split == 1) return launch_single_kind<1, 256, 4>(desc, nt, dev_err, stream);
   return launch_single_kind<3, 128, 3>(desc, nt, dev_err, stream);

@@ -102,6 +102,28 @@ class GemmGroup:
                                            self.kind, ptr(err), stream_handle()), "psgd_gemm_launch")
 
 
+_WORK = {}  # device work lists by (rows, cols, row path, device): built once per shape (read-only afterwards)
+
+
+def _prep_work(rows, cols, normal, dev):
+    key = (rows, cols, normal, dev)
+    w = _WORK.get(key)
+    if w is None:
+        if normal:  # (0, row block)
+            nb = (rows + _capi.PREP_ROWS - 1) // _capi.PREP_ROWS
+            w = torch.stack([torch.zeros(nb, dtype=torch.int32), torch.arange(nb, dtype=torch.int32)], 1)
+        else:  # (0, (ti << 16) | tj) over the 32 x 32 tiles
+            ti = torch.arange((rows + 31) // 32, dtype=torch.int32)
+            tj = torch.arange((cols + 31) // 32, dtype=torch.int32)
+            code = ((ti[:, None] << 16) | tj[None, :]).reshape(-1)
+            w = torch.stack([torch.zeros_like(code), code], 1)
+        w = (w.reshape(-1).to(dev), w.shape[0])
+        if len(_WORK) > 256:
+            _WORK.clear()
+        _WORK[key] = w
+    return w
+
+
 def _prep_one(item_fields, rows, cols, normal, err=None):
     """One psgd_prep launch for a single item (plug-in helpers; item and work list uploaded per call). err: the
     device error word to report into (a fresh one when None)."""
@@ -112,15 +134,11 @@ def _prep_one(item_fields, rows, cols, normal, err=None):
     host = torch.empty(ctypes.sizeof(it), dtype=torch.uint8)
     ctypes.memmove(host.data_ptr(), ctypes.addressof(it), ctypes.sizeof(it))
     items = host.to(dev)
-    if normal:
-        pairs = [(0, rb) for rb in range((rows + _capi.PREP_ROWS - 1) // _capi.PREP_ROWS)]
-    else:
-        pairs = [(0, (ti << 16) | tj) for ti in range((rows + 31) // 32) for tj in range((cols + 31) // 32)]
-    work = torch.tensor([v for p in pairs for v in p], dtype=torch.int32).to(dev)
+    work, nwork = _prep_work(rows, cols, normal, dev)
     hyper = torch.zeros(_capi.HY_COUNT, device=dev)
     if err is None:
         err = torch.zeros(1, dtype=torch.int32, device=dev)
-    check(_capi.lib().psgd_prep(items.data_ptr(), work.data_ptr(), len(pairs), hyper.data_ptr(), err.data_ptr(),
+    check(_capi.lib().psgd_prep(items.data_ptr(), work.data_ptr(), nwork, hyper.data_ptr(), err.data_ptr(),
                                 stream_handle()), "psgd_prep")
     return (items, work, hyper, err)  # kept alive by the caller until the launch has run
 

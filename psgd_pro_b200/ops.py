@@ -126,10 +126,21 @@ def _upload(struct_obj):
     return host.to(torch.device("cuda", torch.cuda.current_device()))
 
 
+_PAIRS = {}  # device work lists of the tile pairs (I <= J) by (n, device), built once per size
+
+
 def _pairs64(n):
-    T = -(-n // _capi.SYM_TILE)
-    flat = [v for I in range(T) for J in range(I, T) for v in (0, (I << 16) | J)]
-    return torch.tensor(flat, dtype=torch.int32).to(torch.device("cuda", torch.cuda.current_device())), len(flat) // 2
+    dev = torch.device("cuda", torch.cuda.current_device())
+    w = _PAIRS.get((n, dev))
+    if w is None:
+        T = -(-n // _capi.SYM_TILE)
+        I, J = torch.triu_indices(T, T).to(torch.int32)
+        code = (I << 16) | J
+        w = (torch.stack([torch.zeros_like(code), code], 1).reshape(-1).to(dev), code.numel())
+        if len(_PAIRS) > 256:
+            _PAIRS.clear()
+        _PAIRS[(n, dev)] = w
+    return w
 
 
 def _sym_item(S, sign):
