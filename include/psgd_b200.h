@@ -105,6 +105,24 @@ int psgd_gemm_launch(const void* dev_table, const uint32_t* dev_tiles, int ntile
 /* Number of SMs the grouped launches use on the current device (grid size of the persistent kernels). */
 int psgd_num_sms(void);
 
+/* Device error word bits (*dev_err of every entry point; bits accumulate until the caller clears the word). */
+#define PSGD_ERR_TIMEOUT_FULL 1    /* a wait for a TMA stage (or the wait probe's barrier) gave up */
+#define PSGD_ERR_TIMEOUT_EMPTY 2   /* a wait for a free stage gave up */
+#define PSGD_ERR_TIMEOUT_ACC 4     /* a wait on an accumulator handoff gave up */
+#define PSGD_ERR_BAD_DESC 8        /* a descriptor failed a device-side check */
+#define PSGD_ERR_NONFINITE 16      /* psgd_factor_update: a factor's L or the Procrustes step came out NaN / Inf */
+
+/* Sets how long the GEMM kernels' waits for work (a TMA stage, a free stage, an accumulator) may take before the
+ * launch gives up and sets PSGD_ERR_TIMEOUT_* (default 2 s; 0 restores it) for launches made after the call;
+ * returns the previous limit. An aborting CTA still waits for its own copies and MMAs in flight with the default
+ * limit before it releases shared memory and TMEM. No counterpart in the reference (it has no device waits). */
+unsigned long long psgd_set_wait_limit_ns(unsigned long long ns);
+
+/* One thread waits, with the library's bounded wait, on a barrier that nothing ever arrives at, for limit_ns
+ * (at most 2 s), then sets PSGD_ERR_TIMEOUT_FULL in *dev_err and returns: the bounded-wait path made to run out,
+ * for tests of the error reporting (the context stays usable). No counterpart in the reference. */
+int psgd_wait_probe(int* dev_err, unsigned long long limit_ns, cudaStream_t stream);
+
 /* Layout check: writes sizeof of PsgdGemmSpec, PsgdPrepItem, PsgdNlbPrepItem, PsgdFactorItem, PsgdSkewItem,
  * PsgdRotItem, PsgdTraceItem, PsgdApplyItem, PsgdBalanceFactor, PsgdBalanceParam, PsgdSymItem, PsgdNlbFinishItem
  * (in this order, at most n of them) and returns how many structs there are (sizes may be NULL to ask). A binding
@@ -195,6 +213,8 @@ int psgd_nlb_prep(const PsgdNlbPrepItem* items, int nitems, int* dev_err, cudaSt
  *   FACTOR_SKEW: s = nf * max_c ||W4_c|| + tiny (the skew bound of R = Q - Q^T); tr(RQ) = sum(part_dot_rq) / s,
  *         tr(RRQ) = -sum(part_dot_sq[0 .. n_sq)) / s^2; a = min(-tr(RQ)/tr(RRQ), 1/8) if tr(RRQ) < 0 else 1/8;
  *         *alpha = a, *beta = 1 / s   (the Procrustes step of psgd_pro_fast.py:141-153). */
+/* Any item whose ell, L, q-update coefficients or Procrustes step come out NaN or infinite sets PSGD_ERR_NONFINITE
+ * (the values are still written, as the reference would carry the NaN on). */
 #define PSGD_FACTOR_DENSE 0
 #define PSGD_FACTOR_RANK1 1
 #define PSGD_FACTOR_DIAG 2

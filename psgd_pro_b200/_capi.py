@@ -135,7 +135,18 @@ SIGNATURES = [
     ("psgd_sym_reduce", c_int, [c_vp, c_int, c_int, c_vp, c_vp]),
     ("psgd_nlb_finish", c_int, [c_vp, c_int, c_vp, c_vp]),
     ("psgd_struct_sizes", c_int, [c_vp, c_int]),
+    ("psgd_set_wait_limit_ns", ctypes.c_ulonglong, [ctypes.c_ulonglong]),
+    ("psgd_wait_probe", c_int, [c_vp, ctypes.c_ulonglong, c_vp]),
 ]
+
+# device error word bits (include/psgd_b200.h PSGD_ERR_*)
+ERR_BITS = {1: "a wait for a TMA stage gave up", 2: "a wait for a free stage gave up",
+            4: "a wait on an accumulator handoff gave up", 8: "a descriptor failed a device-side check",
+            16: "a factor's L or the Procrustes step came out NaN or infinite"}
+
+
+def describe_err(v):
+    return "; ".join(t for b, t in ERR_BITS.items() if v & b) or f"flags {v:#x}"
 
 # the structs in the order psgd_struct_sizes reports them
 STRUCTS = [GemmSpec, PrepItem, NlbPrepItem, FactorItem, SkewItem, RotItem, TraceItem, ApplyItem, BalanceFactor,

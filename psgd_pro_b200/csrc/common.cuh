@@ -18,6 +18,7 @@ enum : int {
   ERR_TIMEOUT_EMPTY = 2,    // TMA warp waited too long for a free stage
   ERR_TIMEOUT_ACC = 4,      // epilogue / MMA waited too long on an accumulator handoff
   ERR_BAD_DESC = 8,         // a descriptor failed a device-side sanity check
+  ERR_NONFINITE = 16,       // a factor's L, step size or norm bound came out NaN or infinite
 };
 
 // A wait gives up after this many nanoseconds of %globaltimer; legitimate waits are microseconds.
@@ -63,20 +64,24 @@ PSGD_DEVI bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase of `bar` with the given parity. Returns false (and raises *abort) when the wait exceeds
-// WAIT_LIMIT_NS or another role of the CTA has already aborted; the caller then unwinds without waiting again.
-PSGD_DEVI bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+// limit_ns or another role of the CTA has already aborted; the caller then unwinds without waiting again.
+PSGD_DEVI bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort, unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63u) == 0) {
       if (*abort) return false;
-      if (global_ns() - t0 > WAIT_LIMIT_NS) {
+      if (global_ns() - t0 > limit_ns) {
         *abort = 1;
         return false;
       }
     }
   }
+}
+
+PSGD_DEVI bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  return mbar_wait_for(bar, parity, abort, WAIT_LIMIT_NS);
 }
 
 // 2-D TMA tile load into this CTA's shared memory, completion counted on `bar` (bytes). No multicast.

@@ -17,6 +17,7 @@
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <atomic>
 #include <queue>
 #include <type_traits>
 #include <vector>
@@ -783,7 +784,7 @@ PSGD_DEVI void get_tile(const GemmDesc* descs, const uint32_t* tiles, int t, int
 // ---- the kernel body ------------------------------------------------------------------------------------------
 template <int SPLIT, int BNMAX, int STAGES, int KIND>
 __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, const uint32_t* __restrict__ tiles,
-                                          int ntiles, int* err) {
+                                          int ntiles, int* err, unsigned long long wait_ns) {
   using C = GemmCfg<SPLIT, BNMAX, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -853,7 +854,7 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
           const uint32_t ph = (g / STAGES) & 1;
           // 64-deep blocks of this stage that hold any of K (no copy is issued past the end)
           const int nsub = min(C::KSUB, (d.s.K - kb * BK * C::KSUB + BK - 1) / BK);
-          if (!mbar_wait(&empty[s], ph ^ 1, abort)) break;
+          if (!mbar_wait_for(&empty[s], ph ^ 1, abort, wait_ns)) break;
           mbar_arrive_expect_tx(&full[s], sub_bytes * (uint32_t)nsub);
           armed[s] += 1;
           for (int j = 0; j < nsub; ++j) {
@@ -890,7 +891,7 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
         const int kb0 = first_kblock(d.s, tm * BM, BK * C::KSUB);
         const int bn = d.s.bn;
         const uint32_t acc = i & 1, aph = (i >> 1) & 1;
-        if (!mbar_wait(&tempty[acc], aph ^ 1, abort)) break;
+        if (!mbar_wait_for(&tempty[acc], aph ^ 1, abort, wait_ns)) break;
         tc_fence_after();
         const uint32_t dt = tmem_base + acc * BNMAX;
         const uint32_t idesc = idesc_bf16_m128(bn);
@@ -898,7 +899,7 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
         for (int kb = kb0; kb < nk; ++kb, ++g) {
           const int s = g % STAGES;
           const uint32_t ph = (g / STAGES) & 1;
-          if (!mbar_wait(&full[s], ph, abort)) {
+          if (!mbar_wait_for(&full[s], ph, abort, wait_ns)) {
             ok = false;
             break;
           }
@@ -939,7 +940,7 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
       const GemmDesc& d = descs[p];
       const uint32_t acc = i & 1, aph = (i >> 1) & 1;
       // the four epilogue warps agree on success before any named barrier, so none can be left waiting there
-      const bool ok = mbar_wait(&tfull[acc], aph, abort);
+      const bool ok = mbar_wait_for(&tfull[acc], aph, abort, wait_ns);
       if (lane == 0) epi_ok[q] = ok ? 1 : 0;
       named_sync(1, 128);
       const bool all_ok = epi_ok[0] && epi_ok[1] && epi_ok[2] && epi_ok[3];
@@ -979,16 +980,17 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
 
 template <int SPLIT, int BNMAX, int STAGES, int KIND>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
-    gemm_group_kernel(const GemmDesc* __restrict__ descs, const uint32_t* __restrict__ tiles, int ntiles, int* err) {
-  gemm_body<SPLIT, BNMAX, STAGES, KIND>(descs, tiles, ntiles, err);
+    gemm_group_kernel(const GemmDesc* __restrict__ descs, const uint32_t* __restrict__ tiles, int ntiles, int* err,
+                      unsigned long long wait_ns) {
+  gemm_body<SPLIT, BNMAX, STAGES, KIND>(descs, tiles, ntiles, err, wait_ns);
 }
 
 // Single problem: the descriptor is a __grid_constant__ parameter and the tile list is implicit.
 template <int SPLIT, int BNMAX, int STAGES, int KIND>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_single_kernel(const __grid_constant__ GemmDesc desc, const uint32_t* __restrict__ tiles, int ntiles,
-                       int* err) {
-  gemm_body<SPLIT, BNMAX, STAGES, KIND>(&desc, tiles, ntiles, err);
+                       int* err, unsigned long long wait_ns) {
+  gemm_body<SPLIT, BNMAX, STAGES, KIND>(&desc, tiles, ntiles, err, wait_ns);
 }
 
 // ---- the pair kernel (tcgen05 cta_group::2) ------------------------------------------------------------------------
@@ -1020,7 +1022,7 @@ constexpr int PBM = 2 * BM;  // rows of a pair tile
 
 template <int BNMAX, int STAGES, int KIND>
 __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ descs, const uint32_t* __restrict__ tiles,
-                                               int* err) {
+                                               int* err, unsigned long long wait_ns) {
   using C = PairCfg<BNMAX, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1090,12 +1092,12 @@ __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ desc
         for (int kb = kb0; kb < nk; ++kb, ++g) {
           const int s = g % STAGES;
           const uint32_t ph = (g / STAGES) & 1;
-          if (!mbar_wait(&empty[s], ph ^ 1, abort)) break;
+          if (!mbar_wait_for(&empty[s], ph ^ 1, abort, wait_ns)) break;
           if (rank == 0) {
             mbar_arrive_expect_tx(&full[s], bytes);
             armed[s] += 1;
             mbar_arrive_cluster_relaxed(mapa_shared(&go[s], 1));
-          } else if (!mbar_wait(&go[s], ph, abort)) {
+          } else if (!mbar_wait_for(&go[s], ph, abort, wait_ns)) {
             break;
           }
           uint8_t* sa = smem + s * C::STAGE_BYTES;
@@ -1124,7 +1126,7 @@ __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ desc
         const int nk = (d.s.K + BK - 1) / BK;
         const int kb0 = first_kblock(d.s, tm * PBM, BK);
         const uint32_t acc = i & 1, aph = (i >> 1) & 1;
-        if (!mbar_wait(&tempty[acc], aph ^ 1, abort)) break;
+        if (!mbar_wait_for(&tempty[acc], aph ^ 1, abort, wait_ns)) break;
         tc_fence_after();
         const uint32_t dt = tmem_base + acc * BNMAX;
         const uint32_t idesc = idesc_bf16_m256(d.s.bn);
@@ -1132,7 +1134,7 @@ __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ desc
         for (int kb = kb0; kb < nk; ++kb, ++g) {
           const int s = g % STAGES;
           const uint32_t ph = (g / STAGES) & 1;
-          if (!mbar_wait(&full[s], ph, abort)) {
+          if (!mbar_wait_for(&full[s], ph, abort, wait_ns)) {
             ok = false;
             break;
           }
@@ -1165,7 +1167,7 @@ __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ desc
       const GemmDesc& d = descs[p];
       const int tm128 = 2 * tm + (int)rank;  // this CTA's 128 rows of the pair tile
       const uint32_t acc = i & 1, aph = (i >> 1) & 1;
-      const bool ok = mbar_wait(&tfull[acc], aph, abort);
+      const bool ok = mbar_wait_for(&tfull[acc], aph, abort, wait_ns);
       if (lane == 0) epi_ok[q] = ok ? 1 : 0;
       named_sync(1, 128);
       const bool all_ok = epi_ok[0] && epi_ok[1] && epi_ok[2] && epi_ok[3];
@@ -1209,8 +1211,9 @@ __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ desc
 
 template <int BNMAX, int STAGES, int KIND>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
-    gemm_pair_kernel(const GemmDesc* __restrict__ descs, const uint32_t* __restrict__ tiles, int* err) {
-  gemm_pair_body<BNMAX, STAGES, KIND>(descs, tiles, err);
+    gemm_pair_kernel(const GemmDesc* __restrict__ descs, const uint32_t* __restrict__ tiles, int* err,
+                     unsigned long long wait_ns) {
+  gemm_pair_body<BNMAX, STAGES, KIND>(descs, tiles, err, wait_ns);
 }
 
 // ---- host side --------------------------------------------------------------------------------------------------
@@ -1363,6 +1366,12 @@ static int num_sms() {
   return n;
 }
 
+// Limit of the GEMM kernels' waits for work (a TMA stage, a free stage, an accumulator), passed to every launch:
+// WAIT_LIMIT_NS unless psgd_set_wait_limit_ns changed it. The waits of an aborting CTA for its own copies and MMAs
+// in flight keep WAIT_LIMIT_NS whatever this is, so shared memory and TMEM are never released under them.
+static std::atomic<unsigned long long> g_wait_limit_ns{WAIT_LIMIT_NS};
+static unsigned long long wait_limit() { return g_wait_limit_ns.load(std::memory_order_relaxed); }
+
 // Raises the dynamic shared-memory limit of a kernel once per device (never inside a graph capture afterwards).
 static bool smem_attr_once(const void* fn, int bytes) {
   static const void* done[64][32] = {};  // per device: kernels already configured
@@ -1385,7 +1394,7 @@ static int launch_group(const GemmDesc* descs, const uint32_t* tiles, int ntiles
   auto k = gemm_group_kernel<SPLIT, BNMAX, STAGES, KIND>;
   if (!smem_attr_once(reinterpret_cast<const void*>(k), C::SMEM_BYTES)) return PSGD_ELAUNCH;
   const int grid = num_sms();  // one CTA per segment of the tile list
-  k<<<grid, GEMM_THREADS, C::SMEM_BYTES, st>>>(descs, tiles, ntiles, err);
+  k<<<grid, GEMM_THREADS, C::SMEM_BYTES, st>>>(descs, tiles, ntiles, err, wait_limit());
   return cudaGetLastError() == cudaSuccess ? PSGD_OK : PSGD_ELAUNCH;
 }
 
@@ -1395,7 +1404,7 @@ static int launch_single(const GemmDesc& desc, const uint32_t* tiles, int ntiles
   auto k = gemm_single_kernel<SPLIT, BNMAX, STAGES, KIND>;
   if (!smem_attr_once(reinterpret_cast<const void*>(k), C::SMEM_BYTES)) return PSGD_ELAUNCH;
   const int grid = ntiles < num_sms() ? ntiles : num_sms();
-  k<<<grid, GEMM_THREADS, C::SMEM_BYTES, st>>>(desc, tiles, ntiles, err);
+  k<<<grid, GEMM_THREADS, C::SMEM_BYTES, st>>>(desc, tiles, ntiles, err, wait_limit());
   return cudaGetLastError() == cudaSuccess ? PSGD_OK : PSGD_ELAUNCH;
 }
 
@@ -1439,7 +1448,7 @@ static int launch_pair(const GemmDesc* descs, const uint32_t* tiles, int* err, c
   using C = PairCfg<PAIR_BN, PAIR_STAGES>;
   auto k = gemm_pair_kernel<PAIR_BN, PAIR_STAGES, KIND>;
   if (!smem_attr_once(reinterpret_cast<const void*>(k), C::SMEM_BYTES)) return PSGD_ELAUNCH;
-  k<<<2 * pair_clusters(), GEMM_THREADS, C::SMEM_BYTES, st>>>(descs, tiles, err);
+  k<<<2 * pair_clusters(), GEMM_THREADS, C::SMEM_BYTES, st>>>(descs, tiles, err, wait_limit());
   return cudaGetLastError() == cudaSuccess ? PSGD_OK : PSGD_ELAUNCH;
 }
 
@@ -1513,6 +1522,11 @@ static int launch_single_kind(const GemmDesc& d, int ntiles, int* err, cudaStrea
 using namespace psgd;
 
 extern "C" int psgd_num_sms(void) { return num_sms(); }
+
+extern "C" unsigned long long psgd_set_wait_limit_ns(unsigned long long ns) {
+  if (ns == 0) ns = WAIT_LIMIT_NS;
+  return g_wait_limit_ns.exchange(ns);
+}
 
 extern "C" size_t psgd_gemm_table_bytes(int nspecs) { return (size_t)(nspecs > 0 ? nspecs : 0) * sizeof(GemmDesc); }
 

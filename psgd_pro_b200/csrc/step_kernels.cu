@@ -450,7 +450,7 @@ constexpr int FAC_SPLIT = PSGD_FAC_SPLIT;
 static_assert(FAC_SPLIT + 1 <= PSGD_FAC_SCRATCH, "factor scratch too small");
 
 __global__ void __launch_bounds__(FAC_THREADS) factor_kernel(const PsgdFactorItem* __restrict__ items,
-                                                            const float* __restrict__ hyper) {
+                                                            const float* __restrict__ hyper, int* __restrict__ err) {
   const PsgdFactorItem& it = items[blockIdx.x / FAC_SPLIT];
   const int c = blockIdx.x % FAC_SPLIT;
   if (c != 0 && it.kind != PSGD_FACTOR_DIAG) return;
@@ -472,6 +472,7 @@ __global__ void __launch_bounds__(FAC_THREADS) factor_kernel(const PsgdFactorIte
       const float coef = lr / L;
       *it.alpha = -coef;
       *it.beta = 1.f + coef * it.term2;
+      if (!isfinite(ell) || !isfinite(L) || !isfinite(coef)) atomicOr(err, ERR_NONFINITE);
     }
   } else if (it.kind == PSGD_FACTOR_DIAG) {  // this range's term1 (kept in p until factor_diag_kernel) and max
     int lo, hi;
@@ -505,13 +506,16 @@ __global__ void __launch_bounds__(FAC_THREADS) factor_kernel(const PsgdFactorIte
       const float a = tr_rrq < 0.f ? fminf(-tr_rq / tr_rrq, amax) : amax;
       *it.alpha = a;
       *it.beta = 1.f / s;
+      // fminf drops a NaN quotient: a non-finite trace or bound is flagged here
+      if (!isfinite(s) || !isfinite(tr_rq) || !isfinite(tr_rrq)) atomicOr(err, ERR_NONFINITE);
     }
   }
 }
 
 // FACTOR_DIAG, second launch: ell = max term1 + term2 over the ranges, L and the update of q and p in this range.
 __global__ void __launch_bounds__(FAC_THREADS) factor_diag_kernel(const PsgdFactorItem* __restrict__ items,
-                                                                 const float* __restrict__ hyper) {
+                                                                 const float* __restrict__ hyper,
+                                                                 int* __restrict__ err) {
   const PsgdFactorItem& it = items[blockIdx.x / FAC_SPLIT];
   if (it.kind != PSGD_FACTOR_DIAG) return;
   const int c = blockIdx.x % FAC_SPLIT;
@@ -529,7 +533,10 @@ __global__ void __launch_bounds__(FAC_THREADS) factor_diag_kernel(const PsgdFact
     it.q[i] = q;
     it.p[i] = q * q;
   }
-  if (c == 0 && threadIdx.x == 0) *it.L = L;
+  if (c == 0 && threadIdx.x == 0) {
+    *it.L = L;
+    if (!isfinite(ell) || !isfinite(L)) atomicOr(err, ERR_NONFINITE);
+  }
 }
 
 // ---- Rn = Q - Q^T ------------------------------------------------------------------------------------------------
@@ -1162,10 +1169,10 @@ extern "C" int psgd_nlb_prep(const PsgdNlbPrepItem* items, int nitems, int* dev_
 
 extern "C" int psgd_factor_update(const PsgdFactorItem* items, int nitems, const float* hyper, int* dev_err,
                                   cudaStream_t stream) {
-  if (!items || !hyper || nitems < 0) return PSGD_EINVAL;
+  if (!items || !hyper || nitems < 0 || !dev_err) return PSGD_EINVAL;
   if (nitems == 0) return PSGD_OK;
-  factor_kernel<<<nitems * FAC_SPLIT, FAC_THREADS, 0, stream>>>(items, hyper);
-  factor_diag_kernel<<<nitems * FAC_SPLIT, FAC_THREADS, 0, stream>>>(items, hyper);
+  factor_kernel<<<nitems * FAC_SPLIT, FAC_THREADS, 0, stream>>>(items, hyper, dev_err);
+  factor_diag_kernel<<<nitems * FAC_SPLIT, FAC_THREADS, 0, stream>>>(items, hyper, dev_err);
   return launched();
 }
 

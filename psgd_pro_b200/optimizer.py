@@ -911,8 +911,13 @@ class KronWhiten:
         return closure_returns
 
     def check_errors(self):
-        """Raises if a kernel recorded a device-side error (a bounded wait that gave up)."""
+        """Raises if a kernel recorded a device-side error: a bounded wait that gave up, or a factor whose L or
+        Procrustes step came out NaN or infinite (a diverging run; the reference would carry the NaN on)."""
         if self._plan is not None:
             e = int(self._plan.err.item())
             if e:
-                raise RuntimeError(f"psgd_pro_b200: device error flags {e:#x}")
+                raise RuntimeError(f"psgd_pro_b200: device error flags {e:#x}: {_capi.describe_err(e)}")
+
+    def clear_errors(self):
+        if self._plan is not None:
+            self._plan.err.zero_()

@@ -10,7 +10,7 @@ HDR = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), 
 
 def declared_symbols():
     src = open(HDR).read()
-    return sorted(set(re.findall(r"^\s*(?:int|size_t|void)\s+(psgd_\w+)\s*\(", src, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|void|unsigned long long)\s+(psgd_\w+)\s*\(", src, re.M)))
 
 
 def test_header_declares_entry_points():
@@ -45,3 +45,12 @@ def test_header_constants_match_binding():
     assert int(defs["PSGD_TRACE_ROWS"]) == _capi.TRACE_ROWS
     assert int(defs["PSGD_FAC_SCRATCH"]) == _capi.FAC_SCRATCH
     assert int(defs["PSGD_APPLY_CHUNK"]) == _capi.APPLY_CHUNK
+
+
+def test_struct_layout_matches_bindings():
+    """The library's struct sizes (psgd_struct_sizes) equal the ctypes mirrors: a stale build is refused at load."""
+    L = _capi.lib()
+    n = L.psgd_struct_sizes(None, 0)
+    sizes = (ctypes.c_longlong * n)()
+    L.psgd_struct_sizes(sizes, n)
+    assert list(sizes) == [ctypes.sizeof(c) for c in _capi.STRUCTS]
