@@ -328,6 +328,13 @@ def sub_workload(name, dev, args, peaks, peak_src, steps, warmup):
     torch.manual_seed(0)
     torch.cuda.manual_seed(0)
     ms, phase_ms = timed_steps(opt, [opt], grads, steps, warmup, lambda: None)
+    # at N > 1 also the data-parallel loop as it runs in training: every rank copies in its whole set of local
+    # gradients (as at N = 1) and the step reduce-scatters them (average over ranks) before the sharded update
+    e2e_rs = None
+    if world > 1:
+        e2e_rs = e2e_reduce_scatter(params, owner, flat, seg, kw, grads, ek, dev, world, barrier)
+        e2e["reduce_scatter"] = e2e_rs
+
     F = sum(falg(tuple(x for x in s if x != 1), args.max_size, max_skew) for s in shapes)
     rec = {"workload": name, "parameter_set": desc, "tensors": len(shapes),
            "params": sum(math.prod(s) for s in shapes), "steps": steps, "warmup": warmup, "ms_per_step": ms,
@@ -461,6 +468,55 @@ def syrk_table(dev, reps=5):
     return out
 
 
+def e2e_reduce_scatter(params, owner, flat, seg, kw, grads, steps, dev, world, barrier):
+    """steps/s of the sharded step with the gradient reduce-scatter fused in, each step's full local gradient set
+    copied from pinned host memory (the next step's copy starts once this step's reduce-scatters have read the
+    buffer) and the clip scales read back."""
+    import torch
+    import torch.distributed as dist
+    from psgd_pro_b200.dist import ShardedKronWhiten
+    opt = ShardedKronWhiten(params, assignment=owner, flat=(flat, seg), reduce_scatter=True, **kw)
+    views = opt.local_grads()
+    host = [g.cpu().pin_memory() for g in grads[0]]
+    met = torch.empty(max(1, len(opt.owned)), dtype=torch.float32).pin_memory()
+    cs, main = torch.cuda.Stream(), torch.cuda.current_stream()
+    for _ in range(2):  # warm-up: plans, first-call costs
+        for h, v in zip(host, views):
+            v.copy_(h, non_blocking=True)
+        opt.step_math(views)
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    copied = torch.cuda.Event()
+    e0.record()
+    for i in range(steps):
+        with torch.cuda.stream(cs):
+            if opt.rs_consumed is not None:
+                cs.wait_event(opt.rs_consumed)
+            for h, v in zip(host, views):
+                v.copy_(h, non_blocking=True)
+            copied.record(cs)
+        main.wait_event(copied)
+        opt.step_math(views)
+        opt.clip_scales_into(met)
+        torch.cuda.current_stream().synchronize()
+        _ = float(met[0])
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    t = torch.tensor([ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    h2d = sum(h.numel() * h.element_size() for h in host) * world
+    for o in opt.inners:
+        o.check_errors()
+    del opt
+    torch.cuda.empty_cache()
+    return {"value": 1000.0 / ms, "unit": "steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": met.numel() * 4,
+            "inputs": "every rank copies in its whole local gradient set (as N = 1 does); the step reduce-scatters "
+                      "it (NCCL, average over ranks) bucket by bucket before each bucket's update"}
+
+
 # ---- the B200 arm ---------------------------------------------------------------------------------------------------
 def main():
     args = parse()
@@ -591,6 +647,13 @@ def main():
     if world > 1:
         e2e["inputs"] = ("each rank copies in the gradients of the parameters it owns (the sharded step reads no "
                          "others, as a reduce-scatter would deliver them); N = 1 copies all of them")
+
+    # at N > 1 also the data-parallel loop as it runs in training: every rank copies in its whole set of local
+    # gradients (as at N = 1) and the step reduce-scatters them (average over ranks) before the sharded update
+    e2e_rs = None
+    if world > 1:
+        e2e_rs = e2e_reduce_scatter(params, owner, flat, seg, kw, grads, ek, dev, world, barrier)
+        e2e["reduce_scatter"] = e2e_rs
 
     F = sum(falg(tuple(x for x in s if x != 1), args.max_size, max_skew) for s in shapes)
     launches = sum(o._plan.launches_per_step(True) for o in inners) * args.steps

@@ -10,7 +10,13 @@ Overlap: a rank's parameters are split into buckets (balanced by FLOPs, the buck
 stepped by its own optimizer (one grouped launch per phase per bucket). When a bucket's step has been enqueued, its
 all-gather (all_gather_into_tensor over that bucket's region of the flat parameter buffer, in place) starts on a
 side stream, so it runs while the later buckets compute; only the last bucket's all-gather is exposed. The step
-returns with the current stream waiting for every all-gather."""
+returns with the current stream waiting for every all-gather.
+
+Reduce-scatter (reduce_scatter=True): the data-parallel gradient reduction is fused into the sharded step instead of
+a separate all-reduce before it. Each rank passes its own local gradients; they sit in a flat buffer laid out like
+the parameters, and per bucket one reduce_scatter_tensor (average over ranks) delivers to each rank the reduced
+gradients of exactly the parameters it owns, which its optimizer then reads in place. All buckets' reduce-scatters
+are issued at the start of the step on the side stream, so bucket b + 1's runs while bucket b computes."""
 import math
 
 import torch
@@ -26,8 +32,8 @@ def _dense(size, numel, max_size, max_skew):
 def falg(shape, max_size=float("inf"), max_skew=1.0):
     """Algorithmic FLOPs of one step for a parameter of this (squeezed) shape: per 2-D dense factor of size n,
     6n^3 + 5nN + 512n^2; per 1-D dense factor 5n^3 + 521n^2; diagonal factors 0 (memory-bound). An order-r
-    parameter (r > 2) counts, per dense factor of size n, the factor work 5n^3 + 512n^2 and its share of the
-    preconditioner applications and term1, 5nN."""
+    parameter (r > 2) counts the same per dense factor: its factor work 6n^3 + 512n^2 and its share 5nN of the two
+    preconditioner applications and term1."""
     shape = [s for s in shape if s != 1]
     N = max(1, math.prod(shape))
     f = 0.0
@@ -132,9 +138,12 @@ class ShardedKronWhiten:
 
     optimizer_factory(params, **kw) builds the per-bucket optimizer (default psgd_pro_b200.KronWhiten); flat=(buffer,
     layout) marks parameters laid out by make_flat_params (in-place all-gathers; the layout's buckets are used);
-    buckets: all-gather buckets per rank when world > 1 (default 4; one when the parameters are not flat-laid)."""
+    buckets: all-gather buckets per rank when world > 1 (default 4; one when the parameters are not flat-laid);
+    reduce_scatter: step_math takes each rank's local gradients and averages them over the ranks itself (see the
+    module docstring); local_grads() gives views of the flat gradient buffer a training loop can fill in place."""
 
-    def __init__(self, params, group=None, assignment=None, flat=None, optimizer_factory=None, buckets=None, **kw):
+    def __init__(self, params, group=None, assignment=None, flat=None, optimizer_factory=None, buckets=None,
+                 reduce_scatter=False, **kw):
         self.params = list(params)
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -169,6 +178,26 @@ class ShardedKronWhiten:
         self.flat = flat
         self._side = None
         self.timing = None  # a list: each step appends its CUDA events (timing_ms() reads them)
+        self.rs = bool(reduce_scatter) and self.world > 1
+        self.rs_consumed = None
+        if self.rs:
+            lay = flat[1] if flat is not None else FlatLayout([tuple(p.shape) for p in self.params], self.owner,
+                                                              self.world, self.bucket_of)
+            self._glay = lay
+            dt, dv = self.params[0].dtype, self.params[0].device
+            self._gflat = torch.zeros(lay.total, dtype=dt, device=dv)  # local gradients, parameter layout
+            self._gviews = [self._gflat[o:o + p.numel()].view(p.shape) for o, p in zip(lay.offset, self.params)]
+            # this rank's reduced gradients: bucket b's chunk at gown_off[b], the owned parameters in layout order
+            self._gown_off, off = [], 0
+            for k in range(self.nbuckets):
+                self._gown_off.append(off)
+                off += lay.seg[k]
+            self._gown = torch.zeros(max(1, off), dtype=dt, device=dv)
+            self._gred = {}
+            for i, (o, b) in enumerate(zip(self.owner, self.bucket_of)):
+                if o == self.rank:
+                    start = self._gown_off[b] + (lay.offset[i] - lay.start[b] - self.rank * lay.seg[b])
+                    self._gred[i] = self._gown[start:start + self.params[i].numel()].view(self.params[i].shape)
         if flat is None and self.world > 1:
             sizes = [p.numel() for p in self.params]
             self._seg = [max(sum(sz for sz, o, b in zip(sizes, self.owner, self.bucket_of) if o == r and b == k)
@@ -194,6 +223,11 @@ class ShardedKronWhiten:
         segs = self.flat[1].seg if self.flat is not None else self._seg
         return sum((self.world - 1) * s * el for s in segs)
 
+    def local_grads(self):
+        """reduce_scatter mode: views of the flat local-gradient buffer, one per parameter (shaped like it). A loop
+        that writes its gradients there (or passes these views to step_math) saves the packing copy."""
+        return list(self._gviews) if self.rs else None
+
     def clip_scales_into(self, host):
         """Copies the per-parameter clip scales of the last step (this rank's parameters, bucket order) into a
         pinned host tensor without waiting (the step's metric)."""
@@ -208,17 +242,28 @@ class ShardedKronWhiten:
         """grads: one per parameter (all ranks pass the full list). draws (tests): the full draw set of
         KronWhiten.step_math; each bucket keeps the coins and normals of its own parameters."""
         grads = list(grads)
-        if self._scale_pending:
-            from .optimizer import init_scale_from_grads
-            scale = init_scale_from_grads(grads, self._damping)
-            for o in self.inners:
-                o.set_init_scale(scale)
-            self._scale_pending = False
         main = torch.cuda.current_stream() if self.world > 1 and self.params[0].is_cuda else None
         ev = None
         if self.timing is not None and main is not None:
             ev = {"start": torch.cuda.Event(enable_timing=True), "gather": []}
             ev["start"].record(main)
+        rs_done = self._reduce_scatter(grads, main) if self.rs else None
+        if self._scale_pending:
+            from .optimizer import init_scale_from_grads
+            if self.rs:  # the reduced gradients of this rank's parameters, then the maximum over the ranks
+                for e in rs_done:
+                    if e is not None:
+                        main.wait_event(e)
+                own = [self._gred[i] for m in self.members for i in m]
+                m4 = 0.0 if not own else max(float(torch.mean(g.to(torch.float64).abs() ** 4)) for g in own)
+                t = torch.tensor([m4], dtype=torch.float64, device=self.params[0].device)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+                scale = (float(t.item()) + self._damping ** 4) ** (-1 / 8)
+            else:
+                scale = init_scale_from_grads(grads, self._damping)
+            for o in self.inners:
+                o.set_init_scale(scale)
+            self._scale_pending = False
         for k, (m, o) in enumerate(zip(self.members, self.opts)):
             if o is not None:
                 d = None
@@ -226,7 +271,13 @@ class ShardedKronWhiten:
                     d = {"update": draws["update"],
                          "coins": [draws["coins"][i] for i in m] if draws["coins"] else [],
                          "normals": [draws["normals"][i] for i in m] if draws["normals"] else []}
-                o.step_math([grads[i] for i in m], draws=d)
+                if self.rs:
+                    if rs_done[k] is not None:
+                        main.wait_event(rs_done[k])
+                    g = [self._gred[i] for i in m]
+                else:
+                    g = [grads[i] for i in m]
+                o.step_math(g, draws=d)
             self._allgather(k, main, ev)
         if main is not None:
             if ev is not None:
@@ -237,6 +288,41 @@ class ShardedKronWhiten:
                 ev["end"] = torch.cuda.Event(enable_timing=True)
                 ev["end"].record(main)
                 self.timing.append(ev)
+
+    def _reduce_scatter(self, grads, main):
+        """Packs the local gradients into the flat buffer (unless they are its views already) and issues every
+        bucket's reduce-scatter (average over the ranks) on the side stream; returns an event per bucket."""
+        for g, v in zip(grads, self._gviews):
+            if g.data_ptr() != v.data_ptr():
+                v.copy_(g.reshape(v.shape))
+        lay = self._glay
+        avg = dist.get_backend(self.group) == "nccl"
+        if main is None:  # CPU tensors (gloo): synchronous
+            for k in range(self.nbuckets):
+                self._rs_bucket(k, lay, avg)
+            return [None] * self.nbuckets
+        if self._side is None:
+            self._side = torch.cuda.Stream(self.params[0].device)
+        self._side.wait_stream(main)
+        done = []
+        with torch.cuda.stream(self._side):
+            for k in range(self.nbuckets):
+                self._rs_bucket(k, lay, avg)
+                e = torch.cuda.Event()
+                e.record(self._side)
+                done.append(e)
+        self.rs_consumed = done[-1]  # the local-gradient buffer may be refilled once this event has completed
+        return done
+
+    def _rs_bucket(self, k, lay, avg):
+        s, seg = lay.start[k], lay.seg[k]
+        out = self._gown[self._gown_off[k]:self._gown_off[k] + seg]
+        region = self._gflat[s:s + self.world * seg]
+        if avg:
+            dist.reduce_scatter_tensor(out, region, op=dist.ReduceOp.AVG, group=self.group)
+        else:  # gloo has no average: sum, then scale
+            dist.reduce_scatter_tensor(out, region, op=dist.ReduceOp.SUM, group=self.group)
+            out.mul_(1.0 / self.world)
 
     def timing_ms(self):
         """Per recorded step (after a synchronize): compute_ms (start to the end of the last bucket's step),

@@ -101,6 +101,46 @@ def test_sharded_step_matches_one_process(flat, onthefly, buckets):
             np.testing.assert_array_equal(a, b)
 
 
+def rs_worker(rank, world, port, out, buckets):
+    """reduce_scatter mode: rank r passes local gradients w_r * g with w = (4, -2), whose average over the two
+    ranks is g exactly (sums of powers of two): every rank must end with the one-process result for g."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        p0, G, D = make_inputs(kw=KW_ONTHEFLY)
+        owner = assignment_for(SHAPES, world, max_skew=float("inf"))
+        it = iter(p0)
+        params, buf, layout = make_flat_params(SHAPES, owner, world, torch.float32, "cpu",
+                                               init=lambda s: torch.from_numpy(next(it)), buckets=buckets,
+                                               max_skew=float("inf"))
+        opt = ShardedKronWhiten(params, assignment=owner, flat=(buf, layout), optimizer_factory=OracleOptimizer,
+                                reduce_scatter=True, **KW_ONTHEFLY)
+        w = 4.0 if rank == 0 else -2.0
+        for step, (g, d) in enumerate(zip(G, D)):
+            local = [torch.from_numpy(x) * w for x in g]
+            if step == 1:  # the loop may also write straight into the optimizer's gradient buffer
+                views = opt.local_grads()
+                for v, x in zip(views, local):
+                    v.copy_(x)
+                local = views
+            opt.step_math(local, draws=d)
+        out[rank] = [p.detach().numpy().copy() for p in params]
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("buckets", [1, 3])
+def test_reduce_scatter_fused_into_the_sharded_step(buckets):
+    ref = single_process_result(KW_ONTHEFLY)
+    mgr = mp.Manager()
+    out = mgr.dict()
+    port = 29700 + (os.getpid() % 200) + buckets
+    mp.spawn(rs_worker, args=(2, port, out, buckets), nprocs=2, join=True)
+    for r in range(2):
+        for a, b in zip(out[r], ref):
+            np.testing.assert_array_equal(a, b)
+
+
 def test_lpt_balance_and_determinism():
     costs = [falg(s, max_skew=float("inf")) for s in SHAPES]
     own = lpt_assign(costs, 4)

@@ -1,4 +1,5 @@
-"""The sharded step on two B200s over NCCL (psgd_pro_b200.dist.ShardedKronWhiten with the real GPU optimizer),
+"""The sharded step on two B200s over NCCL (psgd_pro_b200.dist.ShardedKronWhiten with the real GPU optimizer, with
+and without the fused gradient reduce-scatter),
 against the same step run whole on one GPU: identical parameters and random draws (reference order, supplied),
 bf16 parameters and gradients, the init scale taken on the fly from every parameter's gradient; after the
 all-gather every rank must hold, bit for bit, the parameters of the one-GPU run, and each rank's Q factors must
@@ -47,7 +48,7 @@ def one_gpu(dev):
     return [p.detach().float().cpu() for p in params], [[q.cpu() for q in s["Q"]] for s in opt.state_dict()["state"]]
 
 
-def worker(rank, world, port, outdir):
+def worker(rank, world, port, outdir, rs=False):
     import torch.distributed as dist
     from datetime import timedelta
     from psgd_pro_b200.dist import ShardedKronWhiten, assignment_for, make_flat_params
@@ -62,9 +63,10 @@ def worker(rank, world, port, outdir):
         it = iter(p0)
         params, flat, seg = make_flat_params(SHAPES, owner, world, torch.bfloat16, dev,
                                              init=lambda s: to_dev(next(it), dev))
-        opt = ShardedKronWhiten(params, assignment=owner, flat=(flat, seg), **KW)
+        opt = ShardedKronWhiten(params, assignment=owner, flat=(flat, seg), reduce_scatter=rs, **KW)
+        w = (4.0 if rank == 0 else -2.0) if rs else 1.0  # local gradients whose average is the gradient exactly
         for g, d in zip(G, D):
-            opt.step_math([to_dev(x, dev) for x in g], draws=d)
+            opt.step_math([to_dev(x, dev) * w for x in g], draws=d)
         torch.cuda.synchronize()
         if opt.inner is not None:
             opt.inner.check_errors()
@@ -79,13 +81,15 @@ def worker(rank, world, port, outdir):
         dist.destroy_process_group()
 
 
-def test_two_gpu_sharded_step_equals_one_gpu_step(cuda):
+@pytest.mark.parametrize("rs", [False, True])
+def test_two_gpu_sharded_step_equals_one_gpu_step(cuda, rs):
+    """rs: the ranks pass local gradients (4 g and -2 g) and the step reduce-scatters them itself (average g)."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     ref_p, ref_q = one_gpu(cuda)
     with tempfile.TemporaryDirectory() as d:
-        port = 29600 + os.getpid() % 300
-        mp.spawn(worker, args=(2, port, d), nprocs=2, join=True)
+        port = 29600 + os.getpid() % 300 + (7 if rs else 0)
+        mp.spawn(worker, args=(2, port, d, rs), nprocs=2, join=True)
         outs = [torch.load(os.path.join(d, f"rank{r}.pt")) for r in range(2)]
     owner = outs[0]["owner"]
     assert sorted(set(owner)) == [0, 1]  # both ranks own parameters
