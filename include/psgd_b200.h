@@ -124,8 +124,8 @@ unsigned long long psgd_set_wait_limit_ns(unsigned long long ns);
 int psgd_wait_probe(int* dev_err, unsigned long long limit_ns, cudaStream_t stream);
 
 /* Layout check: writes sizeof of PsgdGemmSpec, PsgdPrepItem, PsgdNlbPrepItem, PsgdFactorItem, PsgdSkewItem,
- * PsgdRotItem, PsgdTraceItem, PsgdApplyItem, PsgdBalanceFactor, PsgdBalanceParam, PsgdSymItem, PsgdNlbFinishItem
- * (in this order, at most n of them) and returns how many structs there are (sizes may be NULL to ask). A binding
+ * PsgdRotItem, PsgdTraceItem, PsgdApplyItem, PsgdBalanceFactor, PsgdBalanceParam, PsgdSymItem, PsgdNlbFinishItem,
+ * PsgdPermuteItem (in this order, at most n of them) and returns how many structs there are (sizes may be NULL to ask). A binding
  * compares them with its own struct definitions once, before its first launch. */
 int psgd_struct_sizes(long long* sizes, int n);
 
@@ -355,6 +355,31 @@ typedef struct PsgdNlbFinishItem {
   const float* nf; const float* part; int slots; int ncols; float* out;
 } PsgdNlbFinishItem;
 int psgd_nlb_finish(const PsgdNlbFinishItem* items, int nitems, int* dev_err, cudaStream_t stream);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * Layout changes of order-r parameters (r >= 3; psgd_pro.py:107-112 exprP, :222-228 exprGs): a tensor with natural
+ * dims d[0..r-1] moves from a source layout to an output layout, both the natural order with at most one mode moved
+ * (to the end, or for the output also to the front), so that the mode a product contracts is the last (mode
+ * products with P) or the first (term1 = the contraction over every other mode) dimension of a row-major matrix.
+ * The caller describes the output layout position by position (omode: the natural mode at each position, outermost
+ * first; odim: its size) and the source by the stride of each natural mode (sstride); scale[m] (a diagonal factor's
+ * q^2, or NULL) multiplies every element by scale[m][i_m] on the way. Outputs (each optional): the operand out_hi /
+ * out_lo (the output as a rows x cols matrix, cols given, row pitch ld_out), out_f32 (unpadded, output layout),
+ * row_sq (sum of squares of each output row; work units are then rows) and part (sum of squares per work unit).
+ * Work entries (item, unit): an output row when row_sq is set, else a chunk of PSGD_PERMUTE_CHUNK output elements. */
+#define PSGD_PERMUTE_MAX_ORDER 8
+#define PSGD_PERMUTE_CHUNK 4096
+typedef struct PsgdPermuteItem {
+  const float* src;
+  int order; int omode[PSGD_PERMUTE_MAX_ORDER];
+  long long odim[PSGD_PERMUTE_MAX_ORDER];
+  long long sstride[PSGD_PERMUTE_MAX_ORDER];
+  const float* scale[PSGD_PERMUTE_MAX_ORDER];
+  long long numel, cols;
+  void* out_hi; void* out_lo; long long ld_out;
+  float* out_f32; float* row_sq; float* part;
+} PsgdPermuteItem;
+int psgd_permute(const PsgdPermuteItem* items, const uint32_t* work, int nwork, int* dev_err, cudaStream_t stream);
 
 /* Clip and apply for one parameter without any device memory from the caller. It has no counterpart in the
  * reference, which always works through torch and so always allocates. It exists for callers that cannot

@@ -99,6 +99,17 @@ class NlbFinishItem(ctypes.Structure):
     _fields_ = [("nf", c_vp), ("part", c_vp), ("slots", c_int), ("ncols", c_int), ("out", c_vp)]
 
 
+PERMUTE_MAX_ORDER = 8
+PERMUTE_CHUNK = 4096
+
+
+class PermuteItem(ctypes.Structure):
+    _fields_ = [("src", c_vp), ("order", c_int), ("omode", c_int * PERMUTE_MAX_ORDER),
+                ("odim", c_ll * PERMUTE_MAX_ORDER), ("sstride", c_ll * PERMUTE_MAX_ORDER),
+                ("scale", c_vp * PERMUTE_MAX_ORDER), ("numel", c_ll), ("cols", c_ll), ("out_hi", c_vp),
+                ("out_lo", c_vp), ("ld_out", c_ll), ("out_f32", c_vp), ("row_sq", c_vp), ("part", c_vp)]
+
+
 PSGD_PREP_NORMAL, PSGD_PREP_TRANS, PSGD_PREP_DIRECT = 0, 1, 2
 PREP_ROWS = 8
 ROT_ROWS = 8
@@ -137,6 +148,7 @@ SIGNATURES = [
     ("psgd_struct_sizes", c_int, [c_vp, c_int]),
     ("psgd_set_wait_limit_ns", ctypes.c_ulonglong, [ctypes.c_ulonglong]),
     ("psgd_wait_probe", c_int, [c_vp, ctypes.c_ulonglong, c_vp]),
+    ("psgd_permute", c_int, [c_vp, c_vp, c_int, c_vp, c_vp]),
 ]
 
 # device error word bits (include/psgd_b200.h PSGD_ERR_*)
@@ -150,7 +162,7 @@ def describe_err(v):
 
 # the structs in the order psgd_struct_sizes reports them
 STRUCTS = [GemmSpec, PrepItem, NlbPrepItem, FactorItem, SkewItem, RotItem, TraceItem, ApplyItem, BalanceFactor,
-           BalanceParam, SymItem, NlbFinishItem]
+           BalanceParam, SymItem, NlbFinishItem, PermuteItem]
 
 
 def _check_layout(L):

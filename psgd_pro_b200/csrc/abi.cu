@@ -7,7 +7,8 @@ extern "C" int psgd_struct_sizes(long long* sizes, int n) {
       (long long)sizeof(PsgdGemmSpec),   (long long)sizeof(PsgdPrepItem),      (long long)sizeof(PsgdNlbPrepItem),
       (long long)sizeof(PsgdFactorItem), (long long)sizeof(PsgdSkewItem),      (long long)sizeof(PsgdRotItem),
       (long long)sizeof(PsgdTraceItem),  (long long)sizeof(PsgdApplyItem),     (long long)sizeof(PsgdBalanceFactor),
-      (long long)sizeof(PsgdBalanceParam), (long long)sizeof(PsgdSymItem),    (long long)sizeof(PsgdNlbFinishItem)};
+      (long long)sizeof(PsgdBalanceParam), (long long)sizeof(PsgdSymItem),    (long long)sizeof(PsgdNlbFinishItem),
+      (long long)sizeof(PsgdPermuteItem)};
   const int count = (int)(sizeof(all) / sizeof(all[0]));
   if (sizes == nullptr) return count;
   for (int i = 0; i < n && i < count; ++i) sizes[i] = all[i];

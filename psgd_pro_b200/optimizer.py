@@ -131,11 +131,20 @@ class _Param:
         self.shape = tuple(shape)
         numel = max(1, math.prod(self.shape))
         self.numel = numel
-        if len(shape) > 2:
-            raise NotImplementedError("psgd_pro_b200.KronWhiten handles 0-d, 1-d and 2-d parameters; got shape "
-                                      f"{tuple(shape)} (squeezed)")
         order = len(shape)
+        if order > _capi.PERMUTE_MAX_ORDER:
+            raise NotImplementedError(f"psgd_pro_b200.KronWhiten handles parameters of order up to "
+                                      f"{_capi.PERMUTE_MAX_ORDER}; got shape {tuple(shape)} (squeezed)")
         s = scale ** (1.0 / order) if order > 0 else scale  # psgd_pro.py:181 (0-d: Scale itself, :170)
+        self.nd = order >= 3
+        if self.nd:  # one factor per dim (psgd_pro.py:185-212); the products run through layout changes
+            self.n1, self.n2 = numel // shape[-1], shape[-1]
+            self.factors = [plan.new_factor("dense" if is_dense(n, numel, plan.max_size, plan.max_skew) else "diag",
+                                            n, s, numel) for n in shape]
+            self.f1 = self.f2 = None
+            self.kind = ("nd",)
+            self._nd_buffers(plan)
+            return
         if order == 2:
             self.n1, self.n2 = shape
             k1 = "dense" if is_dense(self.n1, numel, plan.max_size, plan.max_skew) else "diag"
@@ -172,6 +181,56 @@ class _Param:
         if k == ("none", "dense"):
             self.w = K.operand(n2, 1, dev, sp)
         self.pg32 = torch.empty(n1, n2, device=dev)
+
+    def _nd_buffers(self, plan):
+        """Order-r parameter: the staged gradient x (fp32, natural layout), two fp32 buffers the chain of mode
+        products alternates between, and per dense mode k an operand for its product (the tensor with mode k last,
+        N / d_k x d_k) and one for its term1 (mode k first, d_k x N / d_k); per diagonal mode the row sums of squares
+        of the mode-first layout (its term1)."""
+        dev, sp, N = plan.device, plan.split == 3, self.numel
+        self.x32 = torch.empty(N, device=dev)
+        self.ch = [torch.empty(N, device=dev), torch.empty(N, device=dev)]
+        self.pg32 = torch.empty(self.n1, self.n2, device=dev)
+        self.op_last, self.op_first, self.t1_diag = {}, {}, {}
+        for k, (n, f) in enumerate(zip(self.shape, self.factors)):
+            if f.kind == "dense":
+                self.op_last[k] = K.operand(N // n, n, dev, sp)
+                self.op_first[k] = K.operand(n, N // n, dev, sp)
+            else:
+                self.t1_diag[k] = torch.zeros(1, n, device=dev)
+        self.apart = torch.zeros(cdiv(N, _capi.PERMUTE_CHUNK), device=dev)
+
+
+def _permute_item(src, dims, src_last, dst_mode, dst_first, scales, op=None, out_f32=None, row_sq=None, part=None):
+    """PermuteItem moving a tensor of natural dims `dims` from the layout with mode src_last moved to the end (None:
+    natural) to the one with dst_mode moved to the end, or to the front when dst_first (None: natural)."""
+    r, N = len(dims), math.prod(dims)
+    src_order = [m for m in range(r) if m != src_last] + ([src_last] if src_last is not None else [])
+    stride, st = {}, 1
+    for m in reversed(src_order):
+        stride[m] = st
+        st *= dims[m]
+    if dst_mode is None:
+        out_order = list(range(r))
+    elif dst_first:
+        out_order = [dst_mode] + [m for m in range(r) if m != dst_mode]
+    else:
+        out_order = [m for m in range(r) if m != dst_mode] + [dst_mode]
+    it = _capi.PermuteItem()
+    it.src, it.order, it.numel = src.data_ptr(), r, N
+    for pos, m in enumerate(out_order):
+        it.omode[pos], it.odim[pos] = m, dims[m]
+    for m in range(r):
+        it.sstride[m] = stride[m]
+        it.scale[m] = scales[m].data_ptr() if scales[m] is not None else None
+    it.cols = (N // dims[dst_mode]) if (dst_mode is not None and dst_first) else \
+        (dims[dst_mode] if dst_mode is not None else dims[-1])
+    if op is not None:
+        it.out_hi, it.out_lo, it.ld_out = K.ptr(op[0]), K.ptr(op[1]), op[0].stride(0)
+    it.out_f32 = K.ptr(out_f32)
+    it.row_sq, it.part = K.ptr(row_sq), K.ptr(part)
+    units = (N // it.cols) if row_sq is not None else cdiv(N, _capi.PERMUTE_CHUNK)
+    return it, units
 
 
 class _Plan:
@@ -251,6 +310,11 @@ class _Plan:
                 it.xi = p.xi.data_ptr() if phase == "u" else None
                 it.noise_base = p.xi_off
                 it.n1, it.n2, it.eps = p.n1, p.n2, grad_eps[k]
+                if p.nd:  # order-r parameter: x (with noise and momentum) staged in fp32, natural layout
+                    it.mode, it.out_f32 = PSGD_PREP_DIRECT, p.x32.data_ptr()
+                    items.append(it)
+                    pairs += _tile_pairs(len(items) - 1, p.n1, p.n2)
+                    continue
                 it.p1 = p.f1.p.data_ptr() if p.f1.kind == "diag" else None
                 it.p2 = p.f2.p.data_ptr() if p.f2.kind == "diag" else None
                 if kind == ("dense", "diag"):
@@ -285,6 +349,8 @@ class _Plan:
         # U1, U2: Pg of the noisy gradient
         u1, u2, u3, u3r = [], [], [], []
         for p in P:
+            if p.nd:
+                continue
             n1, n2, f1, f2 = p.n1, p.n2, p.f1, p.f2
             if p.kind == ("dense", "dense"):
                 u1.append(self.spec(p.gop, f2.P, n1, n2, n2, out_hi_t=p.yT[0], out_lo_t=p.yT[1]))
@@ -314,6 +380,10 @@ class _Plan:
                                     diag_out=f2.t_diag))
             if f2.kind == "dense" and f2.rank1:
                 u3r.append(self.spec(f2.qta, p.pg_op, n2, 1, n2, bn=16, out_hi=p.w[0], out_lo=p.w[1]))
+        # order-r parameters: chains of mode products through layout changes; their term1 SYRKs join U3
+        self.nd_u, nd_t1 = self._nd_chain(noisy=True, term1_specs=u3)
+        self.nd_a = self._nd_chain(noisy=False)
+        self.nd_t1 = nd_t1
         # the skinny rank-one products form groups of their own, so the big products' groups can run on CTA pairs
         self.g_u1, self.g_u2, self.g_u3, self.g_u3r = self.group(u1), self.group(u2), self.group(u3), self.group(u3r)
 
@@ -419,6 +489,8 @@ class _Plan:
         # A1, A2: preconditioned gradient of the clean gradient, with sum-of-squares partials
         a1, a2 = [], []
         for p in P:
+            if p.nd:
+                continue
             n1, n2, f1, f2 = p.n1, p.n2, p.f1, p.f2
             if p.kind == ("dense", "dense"):
                 a1.append(self.spec(p.gop, f2.P, n1, n2, n2, out_hi_t=p.yT[0], out_lo_t=p.yT[1]))
@@ -438,7 +510,7 @@ class _Plan:
         # A3: clip + apply
         ai, aw = [], []
         for k, p in enumerate(P):
-            it = _capi.ApplyItem()
+            it = _capi.ApplyItem()  # (an order-r parameter's apart holds the final layout change's chunk sums)
             it.param, it.param_bf16, it.numel = p.param.data_ptr(), int(p.param.dtype == torch.bfloat16), p.numel
             it.pg, it.part, it.nparts, it.scale = p.pg32.data_ptr(), p.apart.data_ptr(), p.apart.numel(), \
                 self.clip[k:k + 1].data_ptr()
@@ -472,6 +544,73 @@ class _Plan:
             wad, nwa = _work(wa, dev)
             self.balance[k] = (_upload(_capi.BalanceFactor, fl, dev),
                                _upload(_capi.BalanceParam, [_capi.BalanceParam(0, len(fl))], dev), wmd, nwm, wad, nwa)
+
+    def _nd_chain(self, noisy, term1_specs=None):
+        """Stages of the order-r parameters' preconditioner application Pg = G x_1 P_1 ... x_r P_r (psgd_pro.py:
+        107-112), all such parameters together: stage j changes every parameter's tensor to the layout with its
+        j-th dense mode (from the last) at the end, as an operand (the diagonal factors' q^2 multiplied in at the
+        first change), then one GEMM group multiplies each by its P (fp32 out, same layout). The last stage brings Pg
+        to what follows: for the update (noisy) one operand per dense mode with that mode first (term1 = its SYRK,
+        appended to term1_specs) and per diagonal mode the row sums of squares of that layout; for the apply the
+        natural fp32 Pg with chunk sums of squares for the clip. Returns ([(permute launch, GEMM group)], final
+        permute launch); a permute launch is (item array, work list, count) or None."""
+        dev = self.device
+        nd = [p for p in self.params if p.nd]
+        if not nd:
+            return [], None
+        per_stage, final = [], []
+        for p in nd:
+            dims = p.shape
+            dense = [k for k in range(len(dims)) if p.factors[k].kind == "dense"][::-1]
+            scales = [f.p if f.kind == "diag" else None for f in p.factors]
+            src, last, pending = p.x32, None, scales
+            for j, k in enumerate(dense):
+                f = p.factors[k]
+                it, units = _permute_item(src, dims, last, k, False, pending, op=p.op_last[k])
+                out = p.ch[j % 2][:p.numel].view(p.numel // dims[k], dims[k])
+                spec = self.spec(p.op_last[k], f.P, p.numel // dims[k], dims[k], dims[k], out_f32=out)
+                while len(per_stage) <= j:
+                    per_stage.append(([], [], []))
+                per_stage[j][0].append(it)
+                per_stage[j][1].append(units)
+                per_stage[j][2].append(spec)
+                src, last, pending = p.ch[j % 2], k, [None] * len(dims)
+            if noisy:
+                for k, f in enumerate(p.factors):
+                    if f.kind == "dense":
+                        it, units = _permute_item(src, dims, last, k, True, pending, op=p.op_first[k])
+                        n, R = dims[k], p.numel // dims[k]
+                        term1_specs.append(self.syrk(p.op_first[k], n, R, out_hi=f.T[0], out_lo=f.T[1],
+                                                     part_row=f.t_rows, diag_out=f.t_diag))
+                    else:
+                        it, units = _permute_item(src, dims, last, k, True, pending, row_sq=p.t1_diag[k][0])
+                        self.t1[f.fidx] = (p.t1_diag[k], 1)
+                    final.append((it, units))
+            else:
+                it, units = _permute_item(src, dims, last, None, False, pending, out_f32=p.pg32, part=p.apart)
+                final.append((it, units))
+
+        def launch_of(items_units):
+            items = [iu[0] for iu in items_units]
+            work = [(i, u) for i, (_, n) in enumerate(items_units) for u in range(n)]
+            w, nw = _work(work, dev)
+            return (_upload(_capi.PermuteItem, items, dev), w, nw)
+        stages = [(launch_of(list(zip(its, us))), self.group(specs)) for its, us, specs in per_stage]
+        return stages, launch_of(final)
+
+    def _permute(self, launch, what):
+        if launch is not None and launch[2] > 0:
+            check(_capi.lib().psgd_permute(launch[0].data_ptr(), launch[1].data_ptr(), launch[2], self.err.data_ptr(),
+                                           K.stream_handle()), what)
+
+    def _run_nd(self, stages, final, tr, tag):
+        for j, (perm, grp) in enumerate(stages):
+            self._permute(perm, "permute")
+            tr(f"{tag}_permute{j}")
+            self._launch(grp)
+            tr(f"{tag}_product{j}")
+        self._permute(final, "permute")
+        tr(f"{tag}_permute_out")
 
     def _nlb_prep(self, fs, skew):
         items = []
@@ -549,6 +688,7 @@ class _Plan:
         tr = trace or (lambda name: None)
         check(L.psgd_prep(self.prep_u_dev.data_ptr(), self.prep_u_work.data_ptr(), self.prep_u_n, hy, err, st), "prep")
         tr("prep")
+        self._run_nd(self.nd_u, self.nd_t1, tr, "nd")
         self._launch(self.g_u1)
         tr("u1")
         self._launch(self.g_u2)
@@ -595,6 +735,7 @@ class _Plan:
         tr = trace or (lambda name: None)
         check(L.psgd_prep(self.prep_a_dev.data_ptr(), self.prep_a_work.data_ptr(), self.prep_a_n, hy, err, st), "prep")
         tr("a_prep")
+        self._run_nd(self.nd_a[0], self.nd_a[1], tr, "a_nd")
         self._launch(self.g_a1)
         tr("a1")
         self._launch(self.g_a2)
@@ -611,13 +752,21 @@ class _Plan:
         out += [(f"nlb_skh{k}", g) for k, g in enumerate(self.g_skh)]
         out += [("S", self.g_u17), ("procrustes", self.g_u20), ("gram", self.g_u22), ("a1", self.g_a1),
                 ("a2", self.g_a2)]
+        out += [(f"nd_product{j}", g) for j, (_, g) in enumerate(self.nd_u)]
+        out += [(f"a_nd_product{j}", g) for j, (_, g) in enumerate(self.nd_a[0])]
         return [(n, g) for n, g in out if g is not None]
 
     def launches_per_step(self, update=True):
         """Kernels of libpsgd_b200.so launched by one step (the RNG fill of the update uses torch's kernels)."""
         n = 3  # prep, clip scale, apply
         groups = [self.g_a1, self.g_a2]
+        nd_perm = lambda stages, final: sum(int(p is not None and p[2] > 0) for p, _ in stages) + \
+            int(final is not None and final[2] > 0)
+        n += nd_perm(*self.nd_a)
+        groups += [g for _, g in self.nd_a[0]]
         if update:
+            n += nd_perm(self.nd_u, self.nd_t1)
+            groups += [g for _, g in self.nd_u]
             n += 1  # prep
             n += int(self.nlb_spd_n > 0) + int(self.nlb_skh_n > 0)  # norm-bound starts
             n += 2 * int(self.fac_n > 0) + 2 * int(self.skf_n > 0)  # factor scalars: two launches each

@@ -51,6 +51,11 @@ SCENARIOS = [
     # the benchmarked path at its own sizes: the factor sizes of the Llama-style set (2048, 256, 5632), a 1-D 2048
     # parameter and an embedding whose 32000 dim exceeds max size 8192 (a diagonal factor); gradients N(0, 1e-3^2)
     # rounded to bf16 values, the init scale taken on the fly, max_skew = inf
+    # order-3 and order-4 parameters (a conv-shaped 16 x 12 x 3 x 3 weight, a squeezed (20, 1, 7, 4), a 3-D
+    # parameter whose 70 dim exceeds max size 64 and gets a diagonal factor) beside a matrix, momentum 0.9
+    dict(name="nd_momentum", shapes=[[16, 12, 3, 3], [20, 1, 7, 4], [70, 6, 5], [24, 10]], steps=3,
+         grad_scale=[1e-2, 2e-2, 1e-2, 1e-2], seed=6, force_balance={2: [0], 3: [2]},
+         kw=dict(preconditioner_max_skew=float("inf"), preconditioner_max_size=64, momentum=0.9, lr_params=1e-2)),
     dict(name="llama_block_bf16", shapes=[[2048, 2048], [256, 2048], [5632, 2048], [2048, 5632], [2048],
                                           [32000, 2048]], steps=3,
          grad_scale=[1e-3] * 6, seed=5, sketch=True, grad_bf16=True,

@@ -8,7 +8,7 @@ import numpy as np
 from oracle import psgd_oracle as O
 
 GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
-SCEN = ["config1", "mixed_inf", "mixed_skew1", "whiten_momentum", "prob_half"]
+SCEN = ["config1", "mixed_inf", "mixed_skew1", "whiten_momentum", "prob_half", "nd_momentum"]
 
 
 def rel(a, b):

@@ -151,3 +151,29 @@ def test_momentum_in_the_staging_kernel(cuda, whiten_grad, update_first, gdt):
         pg = opt._plan.params[k].pg32.cpu().numpy().reshape(np.shape(pre[k]))
         assert rel(pg, pre[k]) < tol
     assert st["counter_m"] == 6
+
+
+def test_order4_conv_weight_matches_oracle(cuda):
+    """A conv-shaped 128 x 64 x 3 x 3 weight (four dense factors, the 3 x 3 ones included, max_skew = inf) and an
+    order-3 parameter with a diagonal mode, in bf16 mode, two steps against the oracle on the same draws."""
+    rng = np.random.default_rng(31)
+    shapes = [(128, 64, 3, 3), (40, 300, 6)]
+    kw = dict(preconditioner_max_skew=float("inf"), preconditioner_max_size=256, preconditioner_init_scale=0.9)
+    p0 = [rng.standard_normal(s, dtype=np.float32) * np.float32(0.05) for s in shapes]
+    ora = O.KronWhitenOracle(p0, dtype=np.float64, **kw)
+    params = [torch.nn.Parameter(torch.from_numpy(p.copy()).to(cuda)) for p in p0]
+    opt = KronWhiten(params, precision="bf16", **kw)
+    for _ in range(2):
+        G = [rng.standard_normal(s, dtype=np.float32) * np.float32(0.01) for s in shapes]
+        d = ora.make_draws(rng, G, coins=[1.0, 1.0])
+        d["update"] = 0.0
+        pre = ora.step(G, d)
+        opt.step_math([torch.from_numpy(g).to(cuda) for g in G], draws=d)
+    torch.cuda.synchronize()
+    opt.check_errors()
+    for k, ((Qo, _), s) in enumerate(zip(ora.QL, opt.state_dict()["state"])):
+        for qo, qg in zip(Qo, s["Q"]):
+            assert rel(qg.cpu().numpy(), qo) < TOL["bf16"]
+        pg = opt._plan.params[k].pg32.cpu().numpy().reshape(np.shape(pre[k]))
+        assert rel(pg, pre[k]) < TOL["bf16"]
+        assert rel(params[k].detach().cpu().numpy(), ora.params[k]) < TOL["bf16"]
