@@ -328,13 +328,6 @@ def sub_workload(name, dev, args, peaks, peak_src, steps, warmup):
     torch.manual_seed(0)
     torch.cuda.manual_seed(0)
     ms, phase_ms = timed_steps(opt, [opt], grads, steps, warmup, lambda: None)
-    # at N > 1 also the data-parallel loop as it runs in training: every rank copies in its whole set of local
-    # gradients (as at N = 1) and the step reduce-scatters them (average over ranks) before the sharded update
-    e2e_rs = None
-    if world > 1:
-        e2e_rs = e2e_reduce_scatter(params, owner, flat, seg, kw, grads, ek, dev, world, barrier)
-        e2e["reduce_scatter"] = e2e_rs
-
     F = sum(falg(tuple(x for x in s if x != 1), args.max_size, max_skew) for s in shapes)
     rec = {"workload": name, "parameter_set": desc, "tensors": len(shapes),
            "params": sum(math.prod(s) for s in shapes), "steps": steps, "warmup": warmup, "ms_per_step": ms,
