@@ -177,7 +177,8 @@ typedef struct PsgdPrepItem {
   float* part_row; float* part_col; float* part_tile;
   float eps;
   long long noise_base;  /* position of element 0 in the generated noise sequence (a multiple of 4) */
-  /* Momentum (psgd_pro.py:334-343), NULL for none: the buffer m (n1 x n2, g's dtype). When m is set, the staged
+  /* Momentum (psgd_pro.py:334-343; psgd_prep_momentum only), NULL for none: the buffer m (n1 x n2, g's dtype).
+   * When m is set, the staged
    * source is the momentum instead of g: if mom_phase == hyper[PSGD_HY_EMA_PHASE] this pass first applies the EMA,
    * m = rn(rn(beta m) + alpha g) with beta = hyper[PSGD_HY_MOM_BETA], alpha = hyper[PSGD_HY_MOM_ALPHA] (rn:
    * rounding to g's dtype, as torch's in-place mul_ and add_ on that dtype), writes m back and stages it; otherwise it
@@ -186,6 +187,10 @@ typedef struct PsgdPrepItem {
 } PsgdPrepItem;
 int psgd_prep(const PsgdPrepItem* items, const uint32_t* work, int nwork, const float* hyper, int* dev_err,
               cudaStream_t stream);
+/* The same honouring the items' momentum fields (m, mom_phase below); psgd_prep ignores them (its kernel is built
+ * without the momentum path, which keeps its register count and occupancy). */
+int psgd_prep_momentum(const PsgdPrepItem* items, const uint32_t* work, int nwork, const float* hyper, int* dev_err,
+                       cudaStream_t stream);
 
 /* Start of the norm lower bound (psgd_pro.py:31-36 spd, :55-60 skh; psgd_pro_fast.py:32-38), one CTA per item:
  * nf = max diag + tiny (spd) or max |A| + tiny (skh), j = argmax row norm (from part_row[row_slots][n]),

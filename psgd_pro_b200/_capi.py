@@ -133,6 +133,7 @@ SIGNATURES = [
                                  ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
     ("psgd_gemm_launch", c_int, [c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp]),
     ("psgd_prep", c_int, [c_vp, c_vp, c_int, c_vp, c_vp, c_vp]),
+    ("psgd_prep_momentum", c_int, [c_vp, c_vp, c_int, c_vp, c_vp, c_vp]),
     ("psgd_nlb_prep", c_int, [c_vp, c_int, c_vp, c_vp]),
     ("psgd_factor_update", c_int, [c_vp, c_int, c_vp, c_vp, c_vp]),
     ("psgd_skew", c_int, [c_vp, c_vp, c_int, c_vp, c_vp]),

@@ -214,6 +214,9 @@ PSGD_DEVI void prep_rows_vec8(const PsgdPrepItem& it, const void* gsrc, long lon
   }
 }
 
+// MOM: the momentum fields of the items are honoured (a separate instantiation, so the staging without momentum
+// keeps its register count and occupancy; psgd_prep launches MOM = false, psgd_prep_momentum MOM = true).
+template <bool MOM>
 __global__ void __launch_bounds__(256) prep_kernel(const PsgdPrepItem* __restrict__ items,
                                                   const uint32_t* __restrict__ work, int nwork,
                                                   const float* __restrict__ hyper) {
@@ -230,8 +233,8 @@ __global__ void __launch_bounds__(256) prep_kernel(const PsgdPrepItem* __restric
   for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
     const PsgdPrepItem& it = items[work[2 * w]];
     // the staged source: g, or the momentum (this pass applies its EMA when the item's phase is this step's)
-    const bool ema = it.m != nullptr && it.mom_phase == ema_phase;
-    const void* src = (it.m != nullptr && !ema) ? it.m : it.g;
+    const bool ema = MOM && it.m != nullptr && it.mom_phase == ema_phase;
+    const void* src = (MOM && it.m != nullptr && !ema) ? it.m : it.g;
     if (it.mode == PSGD_PREP_NORMAL) {  // rows PREP_ROWS * wv .. : 4-element vectors along each row
       const long long r0 = (long long)work[2 * w + 1] * PREP_ROWS;
       const int rows = (int)min((long long)PREP_ROWS, it.n1 - r0);
@@ -242,7 +245,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const PsgdPrepItem* __restric
                        (reinterpret_cast<uintptr_t>(it.out_hi) & 15) == 0 &&
                        (reinterpret_cast<uintptr_t>(it.out_lo) & 15) == 0;
       if (vec) {
-        if (ema) {
+        if (MOM && ema) {
           if (it.g_bf16)
             prep_rows_vec8<true, true>(it, src, r0, rows, damping, gen, k0, k1, mbeta, malpha, prep_stage);
           else
@@ -1156,7 +1159,17 @@ extern "C" int psgd_prep(const PsgdPrepItem* items, const uint32_t* work, int nw
                          cudaStream_t stream) {
   if (!items || !work || !hyper || nwork < 0) return PSGD_EINVAL;
   if (nwork == 0) return PSGD_OK;
-  prep_kernel<<<grid_for(prep_kernel, 256, nwork, PREP_SMEM), 256, PREP_SMEM, stream>>>(items, work, nwork, hyper);
+  prep_kernel<false><<<grid_for(prep_kernel<false>, 256, nwork, PREP_SMEM), 256, PREP_SMEM, stream>>>(items, work,
+                                                                                                       nwork, hyper);
+  return launched();
+}
+
+extern "C" int psgd_prep_momentum(const PsgdPrepItem* items, const uint32_t* work, int nwork, const float* hyper,
+                                  int* dev_err, cudaStream_t stream) {
+  if (!items || !work || !hyper || nwork < 0) return PSGD_EINVAL;
+  if (nwork == 0) return PSGD_OK;
+  prep_kernel<true><<<grid_for(prep_kernel<true>, 256, nwork, PREP_SMEM), 256, PREP_SMEM, stream>>>(items, work,
+                                                                                                     nwork, hyper);
   return launched();
 }
 

@@ -603,7 +603,13 @@ class _Plan:
             check(_capi.lib().psgd_permute(launch[0].data_ptr(), launch[1].data_ptr(), launch[2], self.err.data_ptr(),
                                            K.stream_handle()), what)
 
+    def _prep_fn(self, L):
+        """The staging entry point: with momentum buffers in the items, the one that honours them."""
+        return L.psgd_prep_momentum if self.mom_key and self.mom_key[0] else L.psgd_prep
+
     def _run_nd(self, stages, final, tr, tag):
+        if not stages and final is None:
+            return
         for j, (perm, grp) in enumerate(stages):
             self._permute(perm, "permute")
             tr(f"{tag}_permute{j}")
@@ -686,7 +692,7 @@ class _Plan:
         """The update phases in order; trace(name) (debugging) is called after each launch."""
         L, st, err, hy = _capi.lib(), K.stream_handle(), self.err.data_ptr(), self.hyper.data_ptr()
         tr = trace or (lambda name: None)
-        check(L.psgd_prep(self.prep_u_dev.data_ptr(), self.prep_u_work.data_ptr(), self.prep_u_n, hy, err, st), "prep")
+        check(self._prep_fn(L)(self.prep_u_dev.data_ptr(), self.prep_u_work.data_ptr(), self.prep_u_n, hy, err, st), "prep")
         tr("prep")
         self._run_nd(self.nd_u, self.nd_t1, tr, "nd")
         self._launch(self.g_u1)
@@ -733,7 +739,7 @@ class _Plan:
     def run_apply(self, trace=None):
         L, st, err, hy = _capi.lib(), K.stream_handle(), self.err.data_ptr(), self.hyper.data_ptr()
         tr = trace or (lambda name: None)
-        check(L.psgd_prep(self.prep_a_dev.data_ptr(), self.prep_a_work.data_ptr(), self.prep_a_n, hy, err, st), "prep")
+        check(self._prep_fn(L)(self.prep_a_dev.data_ptr(), self.prep_a_work.data_ptr(), self.prep_a_n, hy, err, st), "prep")
         tr("a_prep")
         self._run_nd(self.nd_a[0], self.nd_a[1], tr, "a_nd")
         self._launch(self.g_a1)
