@@ -289,7 +289,7 @@ def roofline_of(inners, phase_ms, peaks, peak_src):
     # dram__bytes_write.sum) of the one-layer Llama case (the same factor sizes), scaled to this launch by FLOPs
     traffic = None
     if dominant in ("procrustes", "qupdate") and kind == 9:
-        traffic = flops * (3.357e9 / 1.2609e12)
+        traffic = flops * (3.211e9 / 1.2609e12)
     return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
             "traffic": traffic, "traffic_unit": "bytes per launch", "kernel": kernel, "phase": dominant,
             "flops_per_launch": flops, "ms_per_launch": tm,
@@ -510,6 +510,77 @@ def e2e_reduce_scatter(params, owner, flat, seg, kw, grads, steps, dev, world, b
                       "it (NCCL, average over ranks) bucket by bucket before each bucket's update"}
 
 
+def gemm_vs_cublas(dev):
+    """This package's tcgen05 GEMM beside cuBLAS's bf16 GEMM (torch.matmul) on the step's largest shapes, random
+    data, each looped for about 1.5 s so both run under the same 1000 W cap: TFLOP/s, joules per launch (NVML energy
+    counter) and the median SM clock. Epilogues: plain (bf16 out, as cuBLAS), aux (fp32 read and written plus the
+    transposed bf16 copy: the q-update / Procrustes form) and SYRK (the upper tiles only, n^3 useful FLOPs)."""
+    import torch
+    from psgd_pro_b200 import kernels as K
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByIndex(torch.cuda.current_device())
+        energy = lambda: pynvml.nvmlDeviceGetTotalEnergyConsumption(h) / 1000.0
+    except Exception:
+        energy = None
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def loop(fn, flops, seconds=1.5):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        reps = max(5, int(seconds / max(a.elapsed_time(b) * 1e-3, 1e-6)))
+        phys = os.environ["CUDA_VISIBLE_DEVICES"].split(",")[dev.index] if "CUDA_VISIBLE_DEVICES" in os.environ \
+            else dev.index
+        import tempfile
+        clk = ClockSampler(phys, os.path.join(tempfile.gettempdir(), "psgd_gemm_vs_cublas_clocks.csv"))
+        e0 = energy() if energy else None
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        e1 = energy() if energy else None
+        c = clk.stop()
+        ms = a.elapsed_time(b) / reps
+        rec = {"ms": ms, "tflops": flops / ms / 1e9, "sm_mhz": c["sm_mhz"] if c else None}
+        if e0 is not None:
+            rec["J_per_launch"] = (e1 - e0) / reps
+            rec["tflop_per_J"] = flops / rec["J_per_launch"] / 1e12 if rec["J_per_launch"] > 0 else None
+        return rec
+
+    out = []
+    g = torch.Generator(device=dev)
+    g.manual_seed(1)
+    for n in (5632, 8192):
+        A = torch.randn(n, n, device=dev, generator=g).to(torch.bfloat16)
+        B = torch.randn(n, n, device=dev, generator=g).to(torch.bfloat16)
+        C = torch.empty(n, n, device=dev, dtype=torch.bfloat16)
+        Q = torch.randn(n, n, device=dev, generator=g)
+        rec = {"n": n, "cublas_bf16_gemm": loop(lambda: torch.matmul(A, B.T, out=C), 2 * n ** 3)}
+        gp = K.GemmGroup([K.make_spec((A, None), (B, None), n, n, n, bn=256, out_hi=C)], 1, dev)
+        rec["ours_plain"] = loop(lambda: gp.launch(err), 2 * n ** 3)
+        ga = K.GemmGroup([K.make_spec((A, None), (B, None), n, n, n, bn=256, alpha=-1e-3, beta=1.0, aux=Q, out_f32=Q,
+                                      out_hi_t=C)], 1, dev)
+        rec["ours_aux"] = loop(lambda: ga.launch(err), 2 * n ** 3)
+        gs = K.GemmGroup([K.make_spec((A, None), (A, None), n, n, n, bn=256, mode=K.PSGD_GEMM_SYRK, out_hi=C)], 1, dev)
+        rec["ours_syrk_useful"] = loop(lambda: gs.launch(err), n ** 3)
+        rec["kernels"] = {"plain": gp.kind, "aux": ga.kind, "syrk": gs.kind}
+        out.append(rec)
+        del A, B, C, Q, gp, ga, gs
+    torch.cuda.synchronize()
+    if int(err.item()) != 0:
+        raise RuntimeError(f"device error flags {int(err.item()):#x}")
+    torch.cuda.empty_cache()
+    return out
+
+
 # ---- the B200 arm ---------------------------------------------------------------------------------------------------
 def main():
     args = parse()
@@ -676,6 +747,7 @@ def main():
                 if name != args.workload:
                     extra[name] = sub_workload(name, dev, args, peaks, peak_src, st, max(3, args.warmup))
             extra["syrk_config3"] = syrk_table(dev)
+            extra["gemm_vs_cublas"] = gemm_vs_cublas(dev)
     else:
         prec = inners[0].precision if inners else args.precision
     if rank == 0:
