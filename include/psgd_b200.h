@@ -243,7 +243,9 @@ int psgd_factor_update(const PsgdFactorItem* items, int nitems, const float* hyp
  * pairs of PSGD_SKEW_TILE-square tiles (TI <= TJ): one block reads Q[TI, TJ] and Q[TJ, TI] once and writes both
  * Rn tiles. Reductions use 32-wide slots (tiles32 = ceil(n / 32)): part_row[slot][i] (row sums of squares over the
  * block's columns, slot 2 TJ or 2 TI), and per pair part_max (max |Rn|) and part_dot (sum Rn * Q) in entry
- * (2 TI) * tiles32 + 2 TJ. Every other slot stays as the caller left it (zero: consumers sum or max over all). */
+ * (2 TI) * tiles32 + 2 TJ. Every other slot stays as the caller left it (zero: consumers sum or max over all).
+ * The pair's share of sum Rn * Q is taken as (1/2) sum Rn^2 over its two tiles (the identity
+ * sum_ij (Q_ij - Q_ji) Q_ij = (1/2) sum_ij (Q_ij - Q_ji)^2), which has no cancellation. */
 #define PSGD_SKEW_TILE 64
 typedef struct PsgdSkewItem {
   float* q; int n;

@@ -550,7 +550,8 @@ __global__ void __launch_bounds__(FAC_THREADS) factor_diag_kernel(const PsgdFact
 // (2 TI) * tiles32 + 2 TJ; the slots no block writes stay zero.
 constexpr int SK = PSGD_SKEW_TILE;
 
-PSGD_DEVI void st4_split(void* hi, void* lo, long long idx, const float* x, bool vec, int nvalid) {
+// Four values as bf16 hi and lo computed together (fewer live registers in the rank-one skew kernel).
+PSGD_DEVI void st4_split_both(void* hi, void* lo, long long idx, const float* x, bool vec, int nvalid) {
   __align__(8) __nv_bfloat16 h[4], l[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) split_bf16(x[i], h[i], l[i]);
@@ -563,6 +564,33 @@ PSGD_DEVI void st4_split(void* hi, void* lo, long long idx, const float* x, bool
     for (int i = 0; i < nvalid; ++i) {
       H[i] = h[i];
       if (L) L[i] = l[i];
+    }
+  }
+}
+
+// Four values as bf16 hi (two packed conversions) and, only when lo is given, the lo halves bf16(x - hi).
+PSGD_DEVI void st4_split(void* hi, void* lo, long long idx, const float* x, bool vec, int nvalid) {
+  __align__(8) __nv_bfloat162 h2[2];
+  h2[0] = __floats2bfloat162_rn(x[0], x[1]);
+  h2[1] = __floats2bfloat162_rn(x[2], x[3]);
+  const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(h2);
+  __nv_bfloat16* H = reinterpret_cast<__nv_bfloat16*>(hi) + idx;
+  if (vec) {
+    *reinterpret_cast<uint2*>(H) = *reinterpret_cast<const uint2*>(h2);
+  } else {
+    for (int i = 0; i < nvalid; ++i) H[i] = h[i];
+  }
+  if (lo) {
+    __align__(8) __nv_bfloat162 l2[2];
+    const float2 f0 = __bfloat1622float2(h2[0]), f1 = __bfloat1622float2(h2[1]);
+    l2[0] = __floats2bfloat162_rn(x[0] - f0.x, x[1] - f0.y);
+    l2[1] = __floats2bfloat162_rn(x[2] - f1.x, x[3] - f1.y);
+    const __nv_bfloat16* l = reinterpret_cast<const __nv_bfloat16*>(l2);
+    __nv_bfloat16* L = reinterpret_cast<__nv_bfloat16*>(lo) + idx;
+    if (vec) {
+      *reinterpret_cast<uint2*>(L) = *reinterpret_cast<const uint2*>(l2);
+    } else {
+      for (int i = 0; i < nvalid; ++i) L[i] = l[i];
     }
   }
 }
@@ -771,11 +799,17 @@ __global__ void __launch_bounds__(256, 3) skew_kernel(const PsgdSkewItem* __rest
             v[k] = ok ? x - yv[k] : 0.f;
             rs += v[k] * v[k];
             mx = fmaxf(mx, fabsf(v[k]));
-            dsum += v[k] * x;
           }
-          if (FULL || (gi < n && nv > 0)) st4_split(it.r_hi, it.r_lo, (long long)gi * it.ldr + gj0, v, vs, nv);
+          // sum Rn o Q = sum over (i, j) of (Q_ij - Q_ji) Q_ij = (1/2) sum Rn^2: over a pair of tiles that is the
+          // sum of squares of one of its two Rn tiles (half 0), or half of it for a tile on the diagonal
+          if (half == 0) dsum += diag ? 0.5f * rs : rs;
+          if (FULL || (gi < n && nv > 0)) {
+            if constexpr (R1) st4_split_both(it.r_hi, it.r_lo, (long long)gi * it.ldr + gj0, v, vs, nv);
+            else st4_split(it.r_hi, it.r_lo, (long long)gi * it.ldr + gj0, v, vs, nv);
+          }
           if (r1 && (FULL || (gi < n && nv > 0)))  // q^T of the updated q: row gi is the transposed operand above
-            st4_split(it.qt_hi, it.qt_lo, (long long)gi * it.ldqt + gj0, yv, FULL || (nv == 4 && (it.ldqt % 4) == 0), nv);
+            st4_split_both(it.qt_hi, it.qt_lo, (long long)gi * it.ldqt + gj0, yv,
+                           FULL || (nv == 4 && (it.ldqt % 4) == 0), nv);
           rs += __shfl_xor_sync(0xffffffffu, rs, 1);
           rs += __shfl_xor_sync(0xffffffffu, rs, 2);
           rs += __shfl_xor_sync(0xffffffffu, rs, 4);
