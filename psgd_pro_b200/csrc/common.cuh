@@ -96,6 +96,20 @@ PSGD_DEVI void prefetch_tmap(const CUtensorMap* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
 
+// 2-D TMA tile store from this CTA's shared memory to global memory, tracked in the thread's bulk group.
+PSGD_DEVI void tma_store_2d(const CUtensorMap* tmap, const void* smem_src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+PSGD_DEVI void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until the thread's committed bulk stores have finished reading shared memory.
+PSGD_DEVI void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Waits until the thread's committed bulk stores have completed.
+PSGD_DEVI void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Orders this thread's shared-memory writes before later async-proxy (TMA) reads of them.
+PSGD_DEVI void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // ---- tcgen05 -----------------------------------------------------------------------------------------------
 // TMEM allocation is warp-wide; the allocated base address is written to shared memory.
 PSGD_DEVI void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {

@@ -30,10 +30,17 @@ constexpr int GEMM_THREADS = 192;
 struct __align__(64) GemmDesc {
   CUtensorMap ta[2];  // A hi, lo
   CUtensorMap tb[2];  // B hi, lo
+  CUtensorMap tt;     // the transposed bf16 output (out_hi_t; the mirror half of out_hi in SYRK mode), 32 x 32 boxes
   PsgdGemmSpec s;
   int tiles_m, tiles_n;
-  int fast;  // EPI_* kind of the fast epilogue for interior tiles (0: generic only)
+  int fast;    // EPI_* kind of the fast epilogue for interior tiles (0: generic only)
+  int tstore;  // the fast epilogue writes the transposed bf16 output through tt (TMA stores of 32 x 32 blocks)
 };
+
+// Transposed-output blocks of the TMA-store path: one 32 x 32 bf16 block (2 KB, 64-byte rows with the 64-byte
+// swizzle) per epilogue warp, after the staging blocks. Only one-MMA (bf16) kernels have them.
+constexpr int TBLK_BYTES = 32 * 32 * 2;
+constexpr int tblk_offset(int bytes_before) { return (bytes_before + 1023) & ~1023; }
 
 template <int SPLIT, int BNMAX, int STAGES>
 struct GemmCfg {
@@ -49,8 +56,11 @@ struct GemmCfg {
   static constexpr int TMEM_COLS = 2 * BNMAX;
   static constexpr int CTRL_BYTES = 256;  // barriers, TMEM slot, abort flag
   static constexpr int RED_FLOATS = 4 * BNMAX + BNMAX + 32 + 4 * 32 * 36;  // + the staging blocks
-  static constexpr int SMEM_BYTES = 1024 + TILE_BYTES + CTRL_BYTES + RED_FLOATS * 4;
+  static constexpr int TBLK_OFF = tblk_offset(TILE_BYTES + CTRL_BYTES + RED_FLOATS * 4);
+  static constexpr int SMEM_BYTES = 1024 + (SPLIT == 1 ? TBLK_OFF + 4 * TBLK_BYTES : TILE_BYTES + CTRL_BYTES +
+                                                                                       RED_FLOATS * 4);
   static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
+  static_assert(SMEM_BYTES <= 232448, "shared memory beyond the 227 KB per block");
 };
 
 // ---- epilogue ------------------------------------------------------------------------------------------------
@@ -451,9 +461,38 @@ __device__ __forceinline__ void epilogue_tile(const GemmDesc& d, int tm, int tn,
 // EPI_SYRKP: SYRK whose only output is the packed upper triangle (no mirror, no reductions).
 enum : int { EPI_GENERIC = 0, EPI_AUX = 1, EPI_NLB = 2, EPI_PLAIN = 3, EPI_SYRK = 4, EPI_SYRKP = 5 };
 
+// One 32 x 32 chunk of the transposed bf16 output through a TMA store: lane L packs column L of the warp's staging
+// block (scaled) as row L of the warp's transposed block (64-byte rows, 16-byte groups placed by the 64-byte swizzle,
+// which also keeps the warp's shared-memory writes free of bank conflicts), then one lane stores the block at
+// (x, y) = (first accumulator row, first chunk column) of the map. The block is rewritten only after the previous
+// store from it has finished reading it.
+__device__ __forceinline__ void tstore_chunk(const CUtensorMap* tt, uint8_t* tblk, const float* stage, int lane,
+                                             float scale, long long x, long long y) {
+  if (lane == 0) bulk_wait_read_all();
+  __syncwarp();
+  uint32_t w[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(stage[(2 * i) * STG + lane] * scale,
+                                                   stage[(2 * i + 1) * STG + lane] * scale);
+    w[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  uint8_t* rowp = tblk + lane * 64;
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    *reinterpret_cast<uint4*>(rowp + ((k ^ sw) << 4)) = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tt, tblk, (int)x, (int)y);
+    bulk_commit();
+  }
+}
+
 template <int KIND, int BNMAX, bool DG>
 __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn, uint32_t tacc, int q, int lane, float* red,
-                              float* cs, float* misc, float* stage) {
+                              float* cs, float* misc, float* stage, uint8_t* tblk) {
   static_assert(!DG || KIND == EPI_SYRK || KIND == EPI_SYRKP, "diagonal tiles exist in SYRK mode only");
   const PsgdGemmSpec& sd = d.s;
   const long long s_M = sd.M, s_N = sd.N;
@@ -483,6 +522,8 @@ __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn,
   const int et = q * 32 + lane;
   const float alpha = sd.alpha * (sd.alpha_ptr ? __ldg(sd.alpha_ptr) : 1.f);
   const float beta = sd.beta * (sd.beta_ptr ? __ldg(sd.beta_ptr) : 1.f);
+  // the transposed bf16 output (the mirror in SYRK mode) leaves through TMA stores of the staging block
+  const bool tma_t = tblk != nullptr && d.tstore;
   float inv_nf = 1.f;
   if (KIND == EPI_NLB) {  // column scales of the subspace products, in the reference's division order
     inv_nf = 1.f / *sd.cs_nf;
@@ -650,7 +691,9 @@ __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn,
     // transposed pass: the chunk's column j goes to row n0 + c0 + j of the transposed output (for SYRK, the
     // mirror), so each warp store covers 32 consecutive rows: 64 contiguous bytes (bf16) or 128 (fp32).
     if (KIND == EPI_SYRK) {
-      if (out_hi) {
+      if (out_hi && !MASK && tma_t) {
+        tstore_chunk(&d.tt, tblk, stage, lane, alpha, row0, n0 + c0);
+      } else if (out_hi) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const long long col = n0 + c0 + j;
@@ -679,6 +722,9 @@ __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn,
           dsum += (MASK && n0 + c0 + j <= rr) ? 0.f : t;
         }
       }
+    } else if (ht && tma_t) {
+      __syncwarp();
+      tstore_chunk(&d.tt, tblk, stage, lane, 1.f, row0, n0 + c0);
     } else if (ht) {
       __syncwarp();
       float y[32];
@@ -949,23 +995,25 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
       tc_fence_after();
       const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BNMAX;
       float* stg = stage_all + q * 32 * STG;
+      uint8_t* tb = SPLIT == 1 ? smem + C::TBLK_OFF + q * TBLK_BYTES : nullptr;
       const long long m0 = (long long)tm * BM, n0 = (long long)tn * d.s.bn;
       const bool interior = m0 + BM <= d.s.M && n0 + d.s.bn <= d.s.N;
       // the launch's kind (template) picks the one fast path compiled into this kernel; problems of another
       // kind, edge tiles and SYRK tiles on the diagonal take the generic epilogue
       const bool fast = KIND != EPI_GENERIC && d.fast == KIND && interior;
       if constexpr (KIND == EPI_SYRK || KIND == EPI_SYRKP) {
-        if (fast && n0 >= m0 + BM) epilogue_fast<KIND, BNMAX, false>(d, tm, tn, tacc, q, lane, red, cs, misc, stg);
-        else if (fast) epilogue_fast<KIND, BNMAX, true>(d, tm, tn, tacc, q, lane, red, cs, misc, stg);
+        if (fast && n0 >= m0 + BM) epilogue_fast<KIND, BNMAX, false>(d, tm, tn, tacc, q, lane, red, cs, misc, stg, tb);
+        else if (fast) epilogue_fast<KIND, BNMAX, true>(d, tm, tn, tacc, q, lane, red, cs, misc, stg, tb);
         else epilogue_tile<BNMAX, KIND == EPI_GENERIC || KIND == EPI_SYRKP>(d, tm, tn, tacc, q, lane, red, cs, misc, stg);
       } else {
-        if (fast) epilogue_fast<KIND, BNMAX, false>(d, tm, tn, tacc, q, lane, red, cs, misc, stg);
+        if (fast) epilogue_fast<KIND, BNMAX, false>(d, tm, tn, tacc, q, lane, red, cs, misc, stg, tb);
         else epilogue_tile<BNMAX, KIND == EPI_GENERIC || KIND == EPI_SYRKP>(d, tm, tn, tacc, q, lane, red, cs, misc, stg);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
+    if (lane == 0) bulk_wait_all();  // this warp's TMA stores have completed before the block exits
   }
 
   tc_fence_before();
@@ -1014,9 +1062,11 @@ struct PairCfg {
   static constexpr int TMEM_COLS = 2 * BNMAX;
   static constexpr int CTRL_BYTES = 512;
   static constexpr int RED_FLOATS = 4 * BNMAX + BNMAX + 32 + 4 * 32 * 36;
-  static constexpr int SMEM_BYTES = 1024 + TILE_BYTES + CTRL_BYTES + RED_FLOATS * 4;
+  static constexpr int TBLK_OFF = tblk_offset(TILE_BYTES + CTRL_BYTES + RED_FLOATS * 4);
+  static constexpr int SMEM_BYTES = 1024 + TBLK_OFF + 4 * TBLK_BYTES;
   static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
   static_assert((3 * STAGES + 5) * 8 + 8 <= CTRL_BYTES, "barriers must fit the control block");
+  static_assert(SMEM_BYTES <= 232448, "shared memory beyond the 227 KB per block");
 };
 constexpr int PBM = 2 * BM;  // rows of a pair tile
 
@@ -1176,16 +1226,17 @@ __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ desc
       tc_fence_after();
       const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BNMAX;
       float* stg = stage_all + q * 32 * STG;
+      uint8_t* tb = smem + C::TBLK_OFF + q * TBLK_BYTES;
       const long long m0 = (long long)tm128 * BM, n0 = (long long)tn * d.s.bn;
       if (m0 < d.s.M) {
         const bool interior = m0 + BM <= d.s.M && n0 + d.s.bn <= d.s.N;
         const bool fast = KIND != EPI_GENERIC && d.fast == KIND && interior;
         if constexpr (KIND == EPI_SYRK || KIND == EPI_SYRKP) {
-          if (fast && n0 >= m0 + BM) epilogue_fast<KIND, BNMAX, false>(d, tm128, tn, tacc, q, lane, red, cs, misc, stg);
-          else if (fast) epilogue_fast<KIND, BNMAX, true>(d, tm128, tn, tacc, q, lane, red, cs, misc, stg);
+          if (fast && n0 >= m0 + BM) epilogue_fast<KIND, BNMAX, false>(d, tm128, tn, tacc, q, lane, red, cs, misc, stg, tb);
+          else if (fast) epilogue_fast<KIND, BNMAX, true>(d, tm128, tn, tacc, q, lane, red, cs, misc, stg, tb);
           else epilogue_tile<BNMAX, KIND == EPI_GENERIC || KIND == EPI_SYRKP>(d, tm128, tn, tacc, q, lane, red, cs, misc, stg);
         } else {
-          if (fast) epilogue_fast<KIND, BNMAX, false>(d, tm128, tn, tacc, q, lane, red, cs, misc, stg);
+          if (fast) epilogue_fast<KIND, BNMAX, false>(d, tm128, tn, tacc, q, lane, red, cs, misc, stg, tb);
           else epilogue_tile<BNMAX, KIND == EPI_GENERIC || KIND == EPI_SYRKP>(d, tm128, tn, tacc, q, lane, red, cs, misc, stg);
         }
       }
@@ -1196,6 +1247,7 @@ __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ desc
         else mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
       }
     }
+    if (lane == 0) bulk_wait_all();  // this warp's TMA stores have completed before the block exits
   }
 
   tc_fence_before();
@@ -1245,6 +1297,23 @@ static int encode_bf16(CUtensorMap* tm, const void* ptr, int rows, int cols, lon
   cuuint32_t estr[2] = {1u, 1u};
   CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? PSGD_OK : PSGD_ETMAP;
+}
+
+// Store map of a row-major bf16 matrix (rows x cols, leading dimension ld) in 32 x 32 boxes with the 64-byte
+// swizzle (one box row is 64 bytes).
+static int encode_store_bf16(CUtensorMap* tm, const void* ptr, long long rows, long long cols, long long ld) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return PSGD_ETMAP;
+  if (ptr == nullptr || (reinterpret_cast<uintptr_t>(ptr) & 15) || (ld % 8) || ld < cols || rows < 1 || cols < 1)
+    return PSGD_EINVAL;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {32u, 32u};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? PSGD_OK : PSGD_ETMAP;
 }
@@ -1313,6 +1382,18 @@ static int fill_desc(GemmDesc* d, const PsgdGemmSpec& s, int split, bool pair = 
   } else {
     d->ta[1] = d->ta[0];
     d->tb[1] = d->tb[0];
+    // bf16 kernels store the transposed output of the fast epilogue with TMA where its alignment allows
+    const void* tp = nullptr;
+    long long trows = 0, tcols = 0, tld = 0;
+    if ((d->fast == EPI_AUX || d->fast == EPI_PLAIN) && s.out_hi_t && !s.out_lo_t) {
+      tp = s.out_hi_t, trows = s.N, tcols = s.M, tld = s.ld_bt;
+    } else if (d->fast == EPI_SYRK && s.out_hi && !s.out_lo) {
+      tp = s.out_hi, trows = s.N, tcols = s.N, tld = s.ld_b;
+    }
+    const char* env = getenv("PSGD_GEMM_TSTORE");  // "0": the per-lane stores of the transposed output instead
+    const bool want = !(env && env[0] == '0');
+    if (want && tp && al(tp, 16) && tld % 8 == 0 && encode_store_bf16(&d->tt, tp, trows, tcols, tld) == PSGD_OK)
+      d->tstore = 1;
   }
   return PSGD_OK;
 }
