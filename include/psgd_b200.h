@@ -184,6 +184,10 @@ typedef struct PsgdPrepItem {
    * rounding to g's dtype, as torch's in-place mul_ and add_ on that dtype), writes m back and stages it; otherwise it
    * stages m as stored. */
   void* m; int mom_phase;
+  /* PREP_NORMAL only, NULL for none: x before the damping noise is also stored here (bf16 hi / lo halves, the
+   * layout and ld_out of out_hi), so one read of G stages both the noisy operand of the preconditioner update and
+   * the clean operand of the parameter update. */
+  void* out2_hi; void* out2_lo;
 } PsgdPrepItem;
 int psgd_prep(const PsgdPrepItem* items, const uint32_t* work, int nwork, const float* hyper, int* dev_err,
               cudaStream_t stream);

@@ -43,7 +43,7 @@ class PrepItem(ctypes.Structure):
     _fields_ = [("g", c_vp), ("g_bf16", c_int), ("mode", c_int), ("xi", c_vp), ("n1", c_int), ("n2", c_int),
                 ("p1", c_vp), ("p2", c_vp), ("out_hi", c_vp), ("out_lo", c_vp), ("ld_out", c_ll),
                 ("out_f32", c_vp), ("part_row", c_vp), ("part_col", c_vp), ("part_tile", c_vp), ("eps", c_float),
-                ("noise_base", c_ll), ("m", c_vp), ("mom_phase", c_int)]
+                ("noise_base", c_ll), ("m", c_vp), ("mom_phase", c_int), ("out2_hi", c_vp), ("out2_lo", c_vp)]
 
 
 class NlbPrepItem(ctypes.Structure):

@@ -113,6 +113,24 @@ PSGD_DEVI void cp_async16_raw(void* dst, const void* src) {
                : "memory");
 }
 
+// Eight consecutive values as bf16 operand halves at element o: hi = bf16(x) two at a time (packed conversions),
+// lo = bf16(x - hi) only when a lo half is staged (16-byte stores).
+PSGD_DEVI void st8_split(void* out_hi, void* out_lo, long long o, const float* x) {
+  __align__(16) __nv_bfloat162 h[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+  *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(out_hi) + o) = *reinterpret_cast<const uint4*>(h);
+  if (out_lo) {
+    __align__(16) __nv_bfloat162 l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 hf = __bfloat1622float2(h[i]);
+      l[i] = __floats2bfloat162_rn(x[2 * i] - hf.x, x[2 * i + 1] - hf.y);
+    }
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(out_lo) + o) = *reinterpret_cast<const uint4*>(l);
+  }
+}
+
 // EMA: the item's momentum EMA runs in this pass (g is staged through shared memory, m is read into registers for
 // the whole batch before the conversions, and the new m is written back); otherwise `src` (g or m) is staged.
 template <bool BF16, bool EMA>
@@ -185,6 +203,8 @@ PSGD_DEVI void prep_rows_vec8(const PsgdPrepItem& it, const void* gsrc, long lon
 #pragma unroll
         for (int c = 0; c < CH; ++c) mp[c] = mo[c];
       }
+      const long long o = row * it.ld_out + col;
+      if (it.out2_hi) st8_split(it.out2_hi, it.out2_lo, o, x);  // the clean operand, before the damping noise
       if (it.xi) {
 #pragma unroll
         for (int hv = 0; hv < 2; ++hv) {
@@ -195,21 +215,7 @@ PSGD_DEVI void prep_rows_vec8(const PsgdPrepItem& it, const void* gsrc, long lon
           for (int i = 0; i < 4; ++i) x[4 * hv + i] += (damping + it.eps * fabsf(x[4 * hv + i])) * zz[i];
         }
       }
-      // hi = bf16(x) two at a time (packed conversions); lo = bf16(x - hi) only when the item stages lo halves
-      __align__(16) __nv_bfloat162 h[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
-      const long long o = row * it.ld_out + col;
-      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(it.out_hi) + o) = *reinterpret_cast<const uint4*>(h);
-      if (it.out_lo) {
-        __align__(16) __nv_bfloat162 l[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 hf = __bfloat1622float2(h[i]);
-          l[i] = __floats2bfloat162_rn(x[2 * i] - hf.x, x[2 * i + 1] - hf.y);
-        }
-        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(it.out_lo) + o) = *reinterpret_cast<const uint4*>(l);
-      }
+      st8_split(it.out_hi, it.out_lo, o, x);
     }
   }
 }
@@ -243,7 +249,9 @@ __global__ void __launch_bounds__(256) prep_kernel(const PsgdPrepItem* __restric
                        (it.xi == nullptr || (reinterpret_cast<uintptr_t>(it.xi) & 15) == 0) &&
                        (it.noise_base & 3) == 0 && (it.ld_out % 8) == 0 &&
                        (reinterpret_cast<uintptr_t>(it.out_hi) & 15) == 0 &&
-                       (reinterpret_cast<uintptr_t>(it.out_lo) & 15) == 0;
+                       (reinterpret_cast<uintptr_t>(it.out_lo) & 15) == 0 &&
+                       (reinterpret_cast<uintptr_t>(it.out2_hi) & 15) == 0 &&
+                       (reinterpret_cast<uintptr_t>(it.out2_lo) & 15) == 0;
       if (vec) {
         if (MOM && ema) {
           if (it.g_bf16)
@@ -261,6 +269,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const PsgdPrepItem* __restric
           const long long row = r0 + k / it.n2, col = k % it.n2;
           const long long idx = row * it.n2 + col;
           float x = load_src(it, src, ema, idx, mbeta, malpha);
+          if (it.out2_hi) store_split(it.out2_hi, it.out2_lo, row * it.ld_out + col, x);
           if (it.xi) x += (damping + it.eps * fabsf(x)) * (gen ? normal1(it.noise_base + idx, k0, k1) : it.xi[idx]);
           store_split(it.out_hi, it.out_lo, row * it.ld_out + col, x);
         }

@@ -168,8 +168,10 @@ class _Param:
         n1, n2 = self.n1, self.n2
         k = self.kind
         self.gop = self.yT = self.pg_op = self.pgT = self.w = None
+        self.gop_a = None  # the clean operand of the parameter update (PREP_NORMAL parameters)
         if k in (("dense", "dense"), ("diag", "dense"), ("none", "dense")):
             self.gop = K.operand(n1, n2, dev, sp)
+            self.gop_a = K.operand(n1, n2, dev, sp)
         elif k == ("dense", "diag"):
             self.gop = K.operand(n2, n1, dev, sp)
         if k == ("dense", "dense"):
@@ -296,9 +298,12 @@ class _Plan:
         self.grad_ptrs = tuple(t.data_ptr() for t in grads)
         self.mom_key = (ms is not None, bool(whiten_grad))
         self._ptr_items = {}
-        # U0 / A0: gradient staging
+        # U0 / A0: gradient staging. When both passes stage the same source (no momentum, or the momentum in both),
+        # the update's pass also writes the clean operand of PREP_NORMAL parameters (gop_a), and an apply that
+        # follows an update in the same step stages only the other parameters (work list prep_a_rest).
+        self.fuse_stage = ms is None or not whiten_grad
         self.prep_u, self.prep_a = [], []
-        pu, pa = [], []
+        pu, pa, pa_rest = [], [], []
         self.t1 = {}
         for k, p in enumerate(P):
             kind = p.kind
@@ -322,7 +327,10 @@ class _Plan:
                     it.out_hi, it.out_lo, it.ld_out = K.ptr(p.gop[0]), K.ptr(p.gop[1]), p.gop[0].stride(0)
                 elif p.gop is not None:
                     it.mode = PSGD_PREP_NORMAL
-                    it.out_hi, it.out_lo, it.ld_out = K.ptr(p.gop[0]), K.ptr(p.gop[1]), p.gop[0].stride(0)
+                    op = p.gop if phase == "u" else p.gop_a
+                    it.out_hi, it.out_lo, it.ld_out = K.ptr(op[0]), K.ptr(op[1]), op[0].stride(0)
+                    if phase == "u" and self.fuse_stage:
+                        it.out2_hi, it.out2_lo = K.ptr(p.gop_a[0]), K.ptr(p.gop_a[1])
                 else:
                     it.mode = PSGD_PREP_DIRECT
                     if phase == "u":
@@ -338,13 +346,17 @@ class _Plan:
                         it.out_f32, it.part_tile = p.pg32.data_ptr(), p.apart.data_ptr()
                 items.append(it)
                 if it.mode == PSGD_PREP_NORMAL:
-                    pairs += [(len(items) - 1, rb) for rb in range(cdiv(p.n1, _capi.PREP_ROWS))]
+                    w = [(len(items) - 1, rb) for rb in range(cdiv(p.n1, _capi.PREP_ROWS))]
                 else:
-                    pairs += _tile_pairs(len(items) - 1, p.n1, p.n2)
+                    w = _tile_pairs(len(items) - 1, p.n1, p.n2)
+                pairs += w
+                if phase == "a" and not (it.mode == PSGD_PREP_NORMAL and self.fuse_stage):
+                    pa_rest += w
         self.prep_u_dev = _upload(_capi.PrepItem, self.prep_u, dev)
         self.prep_a_dev = _upload(_capi.PrepItem, self.prep_a, dev)
         self.prep_u_work, self.prep_u_n = _work(pu, dev)
         self.prep_a_work, self.prep_a_n = _work(pa, dev)
+        self.prep_a_rest_work, self.prep_a_rest_n = _work(pa_rest, dev)
 
         # U1, U2: Pg of the noisy gradient
         u1, u2, u3, u3r = [], [], [], []
@@ -493,14 +505,14 @@ class _Plan:
                 continue
             n1, n2, f1, f2 = p.n1, p.n2, p.f1, p.f2
             if p.kind == ("dense", "dense"):
-                a1.append(self.spec(p.gop, f2.P, n1, n2, n2, out_hi_t=p.yT[0], out_lo_t=p.yT[1]))
+                a1.append(self.spec(p.gop_a, f2.P, n1, n2, n2, out_hi_t=p.yT[0], out_lo_t=p.yT[1]))
                 bn = choose_bn(n2, split)
                 p.apart = torch.zeros(cdiv(n1, BM) * cdiv(n2, bn), device=dev)
                 a2.append(self.spec(f1.P, p.yT, n1, n2, n1, bn=bn, out_f32=p.pg32, part_tile=p.apart))
             elif p.kind in (("diag", "dense"), ("none", "dense")):
                 bn = choose_bn(n2, split)
                 p.apart = torch.zeros(cdiv(n1, BM) * cdiv(n2, bn), device=dev)
-                a1.append(self.spec(p.gop, f2.P, n1, n2, n2, bn=bn, row_scale=f1.p if f1.kind == "diag" else None,
+                a1.append(self.spec(p.gop_a, f2.P, n1, n2, n2, bn=bn, row_scale=f1.p if f1.kind == "diag" else None,
                                     out_f32=p.pg32, part_tile=p.apart))
             elif p.kind == ("dense", "diag"):
                 bn = choose_bn(n2, split)
@@ -736,10 +748,15 @@ class _Plan:
         self._launch(self.g_u22)
         tr("gram")
 
-    def run_apply(self, trace=None):
+    def run_apply(self, trace=None, after_update=False):
+        """The parameter update. after_update: the update phases ran earlier in this step, so their staging pass
+        already wrote the clean operands it could (fuse_stage) and only the other parameters are staged here."""
         L, st, err, hy = _capi.lib(), K.stream_handle(), self.err.data_ptr(), self.hyper.data_ptr()
         tr = trace or (lambda name: None)
-        check(self._prep_fn(L)(self.prep_a_dev.data_ptr(), self.prep_a_work.data_ptr(), self.prep_a_n, hy, err, st), "prep")
+        work, nwork = (self.prep_a_rest_work, self.prep_a_rest_n) if after_update and self.fuse_stage else \
+            (self.prep_a_work, self.prep_a_n)
+        if nwork:
+            check(self._prep_fn(L)(self.prep_a_dev.data_ptr(), work.data_ptr(), nwork, hy, err, st), "prep")
         tr("a_prep")
         self._run_nd(self.nd_a[0], self.nd_a[1], tr, "a_nd")
         self._launch(self.g_a1)
@@ -762,9 +779,10 @@ class _Plan:
         out += [(f"a_nd_product{j}", g) for j, (_, g) in enumerate(self.nd_a[0])]
         return [(n, g) for n, g in out if g is not None]
 
-    def launches_per_step(self, update=True):
+    def launches_per_step(self, update=True, update_first=True):
         """Kernels of libpsgd_b200.so launched by one step (the RNG fill of the update uses torch's kernels)."""
-        n = 3  # prep, clip scale, apply
+        a_prep = self.prep_a_rest_n if (update and update_first and self.fuse_stage) else self.prep_a_n
+        n = 2 + int(a_prep > 0)  # clip scale, apply, the apply's staging
         groups = [self.g_a1, self.g_a2]
         nd_perm = lambda stages, final: sum(int(p is not None and p[2] > 0) for p, _ in stages) + \
             int(final is not None and final[2] > 0)
@@ -1030,18 +1048,25 @@ class KronWhiten:
                     trace("rng")
             plan.run_update(trace)
 
+        after = update and self.update_preconditioner_first
+
         def app():
-            plan.run_apply(trace)
+            plan.run_apply(trace, after_update=after)
 
         run = (lambda name, fn: self._phase(name, fn)) if use_graph else (lambda name, fn: fn())
         fired = [k for k, c in enumerate(coins) if c]
-        if update and self.update_preconditioner_first:
-            run("update", upd)
+        def bal():
             self._balance(fired)
-        run("apply", app)
+            if trace is not None:
+                trace("balance")
+
+        if after:
+            run("update", upd)
+            bal()
+        run("apply_after_update" if after else "apply", app)
         if update and not self.update_preconditioner_first:
             run("update", upd)
-            self._balance(fired)
+            bal()
         self._steps += 1
 
     def _load_draws(self, normals):
