@@ -3,6 +3,8 @@
 // factors, the Procrustes step size), Rn = Q - Q^T, the Procrustes multiplier, and clip + apply.
 // Grouped: one launch covers every parameter / factor of a phase through a device item array (and a tile work
 // list for the tiled kernels). Reductions are deterministic (fixed-order partials, no atomics).
+#include <atomic>
+
 #include "common.cuh"
 #include "psgd_b200.h"
 
@@ -853,6 +855,224 @@ __global__ void __launch_bounds__(256, 3) skew_kernel(const PsgdSkewItem* __rest
   cp_async_wait<0>();
 }
 
+// ---- Rn = Q - Q^T, block form (2-D factors without the rank-one update) -------------------------------------------
+// The same work entries, outputs and reductions as skew_kernel, with each thread owning whole 4 x 4 blocks: thread
+// (bi, bj) = (t / 16, t % 16) forms block (bi, bj) of D = Rn[TI, TJ] = A - B^T from rows 4 bi .. 4 bi + 3 of A and
+// rows 4 bj .. 4 bj + 3 of B (eight 16-byte shared-memory reads, the transposition in registers) and writes it and
+// its mirror -D^T, block (bj, bi) of Rn[TJ, TI]. No element is read transposed from shared memory. The staged tiles
+// keep 256-byte rows with their 16-byte chunks permuted (chunk c of row r at position c ^ ((r / 4) mod 16)), which
+// makes the cp.async writes, the row reads of A and the block reads of B all free of bank conflicts. Row sums of
+// squares go through shared memory (partials per 4-column block, summed in a fixed order). Entries are pipelined
+// through SK2_STAGES stages; two blocks share an SM.
+constexpr int SK2_STAGES = 3;
+constexpr int SK2_TILE = SK * SK;                                  // floats per staged tile
+constexpr int SK2_SQ = SK * 17;                                    // one partial array: 64 rows x 16 (+1 pad)
+constexpr int SK2_SMEM = (SK2_STAGES * 2 * SK2_TILE + 2 * SK2_SQ) * (int)sizeof(float);
+PSGD_DEVI int sk2_off(int r, int chunk) { return r * SK + ((chunk ^ ((r >> 2) & 15)) << 2); }
+
+PSGD_DEVI void skew2_issue(const PsgdSkewItem* __restrict__ items, const uint32_t* __restrict__ work, int w,
+                           float* stage, int t) {
+  const PsgdSkewItem& it = items[work[2 * w]];
+  const int ti = work[2 * w + 1] >> 16, tj = work[2 * w + 1] & 0xFFFF;
+  const int n = it.n, i0 = ti * SK, j0 = tj * SK, nload = ti == tj ? 4 : 8;
+  const float* q = it.q;
+  const int ch = t & 15, r0 = t >> 4;
+  const bool vec = (n & 3) == 0 && (reinterpret_cast<uintptr_t>(q) & 15) == 0;
+  for (int j = 0; j < nload; ++j) {
+    const int tile = j >> 2, r = r0 + 16 * (j & 3);
+    const int gr = (tile ? j0 : i0) + r, gc = (tile ? i0 : j0) + 4 * ch;
+    float* dst = stage + tile * SK2_TILE + sk2_off(r, ch);
+    if (vec) {  // whole 16-byte chunks: each is inside the matrix or wholly outside (zero-filled)
+      const bool ok = gr < n && gc < n;
+      cp_async16(dst, ok ? q + (long long)gr * n + gc : q, ok);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const bool ok = gr < n && gc + e < n;
+        cp_async4(dst + e, ok ? q + (long long)gr * n + gc + e : q, ok);
+      }
+    }
+  }
+}
+
+// Output staging (interior pairs with 16-byte aligned rows): once every thread holds its block in registers, the
+// stage's tiles are dead, and the bf16 results are written into that space (hi D, hi -D^T, then lo D, lo -D^T in
+// fp32 mode: 8 KB each, 128-byte rows of sixteen 8-byte units, unit u of row r at u ^ ((r / 4) mod 16), free of
+// bank conflicts for both the block writes and the row reads) and leave in 16-byte row chunks.
+PSGD_DEVI int sk2_unit(int r, int u) { return r * 16 + (u ^ ((r >> 2) & 15)); }  // in 8-byte units
+
+PSGD_DEVI uint2 pack4_bf16(const float* x) {
+  const __nv_bfloat162 h0 = __floats2bfloat162_rn(x[0], x[1]), h1 = __floats2bfloat162_rn(x[2], x[3]);
+  return make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
+}
+PSGD_DEVI void lo4(const float* x, float* lo) {  // x - bf16(x), as the split stores it
+#pragma unroll
+  for (int i = 0; i < 4; ++i) lo[i] = x[i] - __bfloat162float(__float2bfloat16_rn(x[i]));
+}
+
+__global__ void __launch_bounds__(256, 2) skew2_kernel(const PsgdSkewItem* __restrict__ items,
+                                                       const uint32_t* __restrict__ work, int nwork) {
+  extern __shared__ __align__(16) float sk2_smem[];
+  float* const sq0 = sk2_smem + SK2_STAGES * 2 * SK2_TILE;  // [row of D][bj]: row sums over 4-column blocks
+  float* const sq1 = sq0 + SK2_SQ;                          // [row of -D^T][bi]
+  __shared__ float red[8][2];
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
+  const int bi = t >> 4, bj = t & 15;
+  int wnext = blockIdx.x;
+  for (int st = 0; st < SK2_STAGES; ++st, wnext += gridDim.x) {
+    if (wnext < nwork) skew2_issue(items, work, wnext, sk2_smem + st * 2 * SK2_TILE, t);
+    cp_async_commit();
+  }
+  int st = 0;
+  for (int w = blockIdx.x; w < nwork; w += gridDim.x, wnext += gridDim.x, st = st + 1 == SK2_STAGES ? 0 : st + 1) {
+    const PsgdSkewItem& it = items[work[2 * w]];
+    const int ti = work[2 * w + 1] >> 16, tj = work[2 * w + 1] & 0xFFFF;
+    const int n = it.n, i0 = ti * SK, j0 = tj * SK;
+    const bool diag = ti == tj;
+    float* const sA = sk2_smem + st * 2 * SK2_TILE;
+    const float* const sB = diag ? sA : sA + SK2_TILE;
+    cp_async_wait<SK2_STAGES - 1>();  // this entry's group is complete (later groups may still be in flight)
+    __syncthreads();
+    float d[4][4];  // d[r][c] = A[4 bi + r][4 bj + c] - B[4 bj + c][4 bi + r]
+    {
+      float4 a[4], b[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) a[r] = *reinterpret_cast<const float4*>(sA + sk2_off(4 * bi + r, bj));
+#pragma unroll
+      for (int c = 0; c < 4; ++c) b[c] = *reinterpret_cast<const float4*>(sB + sk2_off(4 * bj + c, bi));
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const float ar[4] = {a[r].x, a[r].y, a[r].z, a[r].w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float bc[4] = {b[c].x, b[c].y, b[c].z, b[c].w};
+          d[r][c] = ar[c] - bc[r];
+        }
+      }
+    }
+    // elements outside the matrix were staged as zeros on both sides, so they contribute 0 to every reduction
+    float mx = 0.f, rsum[4], csum[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      rsum[r] = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float v2 = d[r][c] * d[r][c];
+        rsum[r] += v2;
+        csum[c] += v2;
+        mx = fmaxf(mx, fabsf(d[r][c]));
+      }
+    }
+    // sum Rn o Q over the pair = (1/2) sum Rn^2 over its two tiles = sum D^2 (a tile on the diagonal: half of it)
+    float dsum = ((rsum[0] + rsum[1]) + rsum[2]) + rsum[3];
+    if (diag) dsum *= 0.5f;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) sq0[(4 * bi + r) * 17 + bj] = rsum[r];
+    if (!diag) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) sq1[(4 * bj + c) * 17 + bi] = csum[c];
+    }
+    mx = warp_max(mx);
+    dsum = warp_sum(dsum);
+    if (lane == 0) {
+      red[wid][0] = mx;
+      red[wid][1] = dsum;
+    }
+    const bool lo = it.r_lo != nullptr;
+    // Rn[TI, TJ] rows i0 + 4 bi + r, columns j0 + 4 bj ..; Rn[TJ, TI] rows j0 + 4 bj + c, columns i0 + 4 bi ..
+    const bool staged = i0 + SK <= n && j0 + SK <= n && (it.ldr % 8) == 0 &&
+                        (reinterpret_cast<uintptr_t>(it.r_hi) & 15) == 0 &&
+                        (reinterpret_cast<uintptr_t>(it.r_lo) & 15) == 0;
+    __syncthreads();  // the stage's tiles are dead: reuse it for the outputs; partials and red are complete
+    if (staged) {
+      uint2* const ou = reinterpret_cast<uint2*>(sA);  // four 8 KB tiles of 1024 units
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        ou[sk2_unit(4 * bi + r, bj)] = pack4_bf16(d[r]);
+        if (lo) {
+          float l[4];
+          lo4(d[r], l);
+          ou[2048 + sk2_unit(4 * bi + r, bj)] = pack4_bf16(l);
+        }
+      }
+      if (!diag) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float m[4] = {-d[0][c], -d[1][c], -d[2][c], -d[3][c]};
+          ou[1024 + sk2_unit(4 * bj + c, bi)] = pack4_bf16(m);
+          if (lo) {
+            float l[4];
+            lo4(m, l);
+            ou[3072 + sk2_unit(4 * bj + c, bi)] = pack4_bf16(l);
+          }
+        }
+      }
+      __syncthreads();
+      // 16-byte row chunks: thread t takes chunk t % 8 of rows t / 8 and t / 8 + 32 of each tile it writes
+      const int k = t & 7;
+#pragma unroll
+      for (int o = 0; o < 4; ++o) {
+        if ((o & 1) && diag) continue;
+        if ((o & 2) && !lo) continue;
+        const int row0 = (o & 1) ? j0 : i0, col0 = (o & 1) ? i0 : j0;
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>((o & 2) ? it.r_lo : it.r_hi);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int R = (t >> 3) + 32 * h, f = (R >> 2) & 15;
+          uint4 v = reinterpret_cast<const uint4*>(sA)[o * 512 + R * 8 + (k ^ (f >> 1))];
+          if (f & 1) v = make_uint4(v.z, v.w, v.x, v.y);
+          *reinterpret_cast<uint4*>(dst + (long long)(row0 + R) * it.ldr + col0 + 8 * k) = v;
+        }
+      }
+    } else {
+      {
+        const int col = j0 + 4 * bj, nv = max(0, min(4, n - col));
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int row = i0 + 4 * bi + r;
+          if (row < n && nv > 0)
+            st4_split(it.r_hi, it.r_lo, (long long)row * it.ldr + col, d[r], nv == 4 && (it.ldr % 4) == 0, nv);
+        }
+      }
+      if (!diag) {
+        const int col = i0 + 4 * bi, nv = max(0, min(4, n - col));
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int row = j0 + 4 * bj + c;
+          const float m[4] = {-d[0][c], -d[1][c], -d[2][c], -d[3][c]};
+          if (row < n && nv > 0)
+            st4_split(it.r_hi, it.r_lo, (long long)row * it.ldr + col, m, nv == 4 && (it.ldr % 4) == 0, nv);
+        }
+      }
+    }
+    if (t < 2 * SK) {  // row sums: threads 0..63 the rows of Rn[TI, TJ], 64..127 those of Rn[TJ, TI]
+      const int h = t >> 6, r = t & (SK - 1);
+      const int gi = (h ? j0 : i0) + r;
+      if ((h == 0 || !diag) && gi < n) {
+        const float* p = (h ? sq1 : sq0) + r * 17;
+        float acc = 0.f;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) acc += p[k];
+        it.part_row[(long long)(2 * (h ? ti : tj)) * n + gi] = acc;
+      }
+    }
+    if (t == 0) {
+      const int tiles32 = (n + 31) / 32;
+      float m = 0.f, dd = 0.f;
+      for (int k = 0; k < 8; ++k) {
+        m = fmaxf(m, red[k][0]);
+        dd += red[k][1];
+      }
+      it.part_max[(long long)(2 * ti) * tiles32 + 2 * tj] = m;
+      it.part_dot[(long long)(2 * ti) * tiles32 + 2 * tj] = dd;
+    }
+    __syncthreads();  // the stage, the partials and red are free: refill the stage with a later entry
+    if (wnext < nwork) skew2_issue(items, work, wnext, sA, t);
+    cp_async_commit();
+  }
+  cp_async_wait<0>();
+}
+
 // ---- M = a Rn / s + a^2 / 2 (S / s) / s ----------------------------------------------------------------------------
 // Rows of the padded n x ld bf16 arrays, 8 values (16 bytes) per vector; padding columns are zero and stay zero.
 // Work entries: (item, first row of a block of ROT_ROWS rows). Each thread takes up to ROT_VEC vectors per pass
@@ -1236,8 +1456,15 @@ extern "C" int psgd_skew(const PsgdSkewItem* items, const uint32_t* work, int nw
                          cudaStream_t stream) {
   if (!items || !work || nwork < 0) return PSGD_EINVAL;
   if (nwork == 0) return PSGD_OK;
-  if (!skew_smem_attr<false>()) return PSGD_ELAUNCH;
-  skew_kernel<false><<<grid_for(skew_kernel<false>, 256, nwork, SK_SMEM), 256, SK_SMEM, stream>>>(items, work, nwork);
+  static std::atomic<bool> attr_done[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PSGD_ELAUNCH;
+  if (!attr_done[dev].load()) {  // the dynamic shared-memory limit, once per device (before any graph capture)
+    if (cudaFuncSetAttribute(skew2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SK2_SMEM) != cudaSuccess)
+      return PSGD_ELAUNCH;
+    attr_done[dev].store(true);
+  }
+  skew2_kernel<<<grid_for(skew2_kernel, 256, nwork, SK2_SMEM), 256, SK2_SMEM, stream>>>(items, work, nwork);
   return launched();
 }
 
