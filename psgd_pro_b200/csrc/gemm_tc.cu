@@ -827,6 +827,61 @@ PSGD_DEVI void get_tile(const GemmDesc* descs, const uint32_t* tiles, int t, int
   }
 }
 
+// The fields of its tiles the producer and the MMA issuer need, requested one tile ahead (and the tile-list entry two tiles ahead),
+// so the global-memory latency of the next tile's metadata is hidden behind the current tile's MMAs instead of
+// idling the tensor pipe between tiles. (The loads stay where they are written: every mbarrier wait and MMA
+// between them is an asm statement with a memory clobber.)
+struct TileMeta {
+  long long K;
+  int mode, bn, p, tm, tn;
+};
+struct TileAhead {
+  const GemmDesc* descs;
+  const uint32_t* tiles;
+  int t, t_end, t_step;
+  uint32_t e0, e1;  // list entry of tile t (when there is a list)
+  TileMeta m;       // fields of the tile before t
+  PSGD_DEVI TileAhead(const GemmDesc* d, const uint32_t* tl, int t0, int t1, int step)
+      : descs(d), tiles(tl), t(t0), t_end(t1), t_step(step), e0(0), e1(0), m{0, 0, 0, 0, 0, 0} {
+    if (t < t_end) {
+      if (tiles) {
+        e0 = tiles[2 * t];
+        e1 = tiles[2 * t + 1];
+      }
+      m = fetch();
+      advance_entry();
+    }
+  }
+  PSGD_DEVI TileMeta fetch() const {
+    int p, tm, tn;
+    if (tiles) {
+      p = (int)e0;
+      tm = (int)(e1 >> 16);
+      tn = (int)(e1 & 0xFFFF);
+    } else {
+      get_tile(descs, nullptr, t, p, tm, tn);
+    }
+    const PsgdGemmSpec& s = descs[p].s;
+    return TileMeta{s.K, s.mode, s.bn, p, tm, tn};
+  }
+  PSGD_DEVI void advance_entry() {  // t moves to the next tile; its list entry is requested
+    t += t_step;
+    if (tiles && t < t_end) {
+      e0 = tiles[2 * t];
+      e1 = tiles[2 * t + 1];
+    }
+  }
+  // Returns the current tile's fields and requests the next tile's (and the entry of the one after it).
+  PSGD_DEVI TileMeta next() {
+    const TileMeta cur = m;
+    if (t < t_end) {
+      m = fetch();
+      advance_entry();
+    }
+    return cur;
+  }
+};
+
 // ---- the kernel body ------------------------------------------------------------------------------------------
 template <int SPLIT, int BNMAX, int STAGES, int KIND>
 __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, const uint32_t* __restrict__ tiles,
@@ -888,18 +943,20 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
       uint32_t armed[STAGES];  // phases armed per stage, to drain in-flight copies on abort
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) armed[s] = 0;
+      TileAhead ta(descs, tiles, t_begin, t_end, t_step);
       for (int t = t_begin; t < t_end && !*abort; t += t_step) {
-        int p, tm, tn;
-        get_tile(descs, tiles, t, p, tm, tn);
-        const GemmDesc& d = descs[p];
-        const int nk = (d.s.K + BK * C::KSUB - 1) / (BK * C::KSUB);
-        const int kb0 = first_kblock(d.s, tm * BM, BK * C::KSUB);
-        const uint32_t sub_bytes = C::NOPS * (C::A_BYTES + d.s.bn * BK * 2);
+        const TileMeta cur = ta.next();
+        const GemmDesc& d = descs[cur.p];  // (only its tensor maps' addresses are taken below)
+        const int tm = cur.tm, tn = cur.tn, bn = cur.bn;
+        const long long K = cur.K;
+        const int nk = (int)((K + BK * C::KSUB - 1) / (BK * C::KSUB));
+        const int kb0 = cur.mode == PSGD_GEMM_TRMM ? (int)((long long)tm * BM / (BK * C::KSUB)) : 0;
+        const uint32_t sub_bytes = C::NOPS * (C::A_BYTES + bn * BK * 2);
         for (int kb = kb0; kb < nk; ++kb, ++g) {
           const int s = g % STAGES;
           const uint32_t ph = (g / STAGES) & 1;
           // 64-deep blocks of this stage that hold any of K (no copy is issued past the end)
-          const int nsub = min(C::KSUB, (d.s.K - kb * BK * C::KSUB + BK - 1) / BK);
+          const int nsub = (int)min((long long)C::KSUB, (K - (long long)kb * BK * C::KSUB + BK - 1) / BK);
           if (!mbar_wait_for(&empty[s], ph ^ 1, abort, wait_ns)) break;
           mbar_arrive_expect_tx(&full[s], sub_bytes * (uint32_t)nsub);
           armed[s] += 1;
@@ -908,10 +965,10 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
             uint8_t* sb = sa + C::NOPS * C::A_BYTES;
             const int x = (kb * C::KSUB + j) * BK;
             tma_load_2d(sa, &d.ta[0], &full[s], x, tm * BM);
-            tma_load_2d(sb, &d.tb[0], &full[s], x, tn * d.s.bn);
+            tma_load_2d(sb, &d.tb[0], &full[s], x, tn * bn);
             if (SPLIT != 1) {
               tma_load_2d(sa + C::A_BYTES, &d.ta[1], &full[s], x, tm * BM);
-              tma_load_2d(sb + C::B_BYTES, &d.tb[1], &full[s], x, tn * d.s.bn);
+              tma_load_2d(sb + C::B_BYTES, &d.tb[1], &full[s], x, tn * bn);
             }
           }
         }
@@ -929,13 +986,13 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
       // ---------------- MMA issuer ----------------
       uint32_t g = 0, i = 0;
       bool issued = false;
+      TileAhead ta(descs, tiles, t_begin, t_end, t_step);
       for (int t = t_begin; t < t_end; t += t_step, ++i) {
-        int p, tm, tn;
-        get_tile(descs, tiles, t, p, tm, tn);
-        const GemmDesc& d = descs[p];
-        const int nk = (d.s.K + BK * C::KSUB - 1) / (BK * C::KSUB);
-        const int kb0 = first_kblock(d.s, tm * BM, BK * C::KSUB);
-        const int bn = d.s.bn;
+        const TileMeta cur = ta.next();  // this tile's fields; the next tile's are requested here
+        const long long K = cur.K;
+        const int nk = (int)((K + BK * C::KSUB - 1) / (BK * C::KSUB));
+        const int kb0 = cur.mode == PSGD_GEMM_TRMM ? (int)((long long)cur.tm * BM / (BK * C::KSUB)) : 0;
+        const int bn = cur.bn;
         const uint32_t acc = i & 1, aph = (i >> 1) & 1;
         if (!mbar_wait_for(&tempty[acc], aph ^ 1, abort, wait_ns)) break;
         tc_fence_after();
@@ -950,7 +1007,7 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
             break;
           }
           tc_fence_after();
-          const int nsub = min(C::KSUB, (d.s.K - kb * BK * C::KSUB + BK - 1) / BK);
+          const int nsub = (int)min((long long)C::KSUB, (K - (long long)kb * BK * C::KSUB + BK - 1) / BK);
           for (int j = 0; j < nsub; ++j) {
             const uint32_t a_hi = smem_u32(smem + s * C::STAGE_BYTES + j * C::SUB_BYTES);
             const uint32_t b_hi = a_hi + C::NOPS * C::A_BYTES;
@@ -1131,13 +1188,14 @@ __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ desc
       uint32_t armed[STAGES];  // rounds the leader armed per stage, drained on abort
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) armed[s] = 0;
+      TileAhead ta(descs, tiles, t_begin, t_end, 1);
       for (int t = t_begin; t < t_end && !*abort; ++t) {
-        int p, tm, tn;
-        get_tile(descs, tiles, t, p, tm, tn);
-        const GemmDesc& d = descs[p];
-        const int nk = (d.s.K + BK - 1) / BK;
-        const int kb0 = first_kblock(d.s, tm * PBM, BK);
-        const int half = d.s.bn / 2;
+        const TileMeta cur = ta.next();
+        const GemmDesc& d = descs[cur.p];  // (only its tensor maps' addresses are taken below)
+        const int tm = cur.tm, tn = cur.tn, bn = cur.bn;
+        const int nk = (int)((cur.K + BK - 1) / BK);
+        const int kb0 = cur.mode == PSGD_GEMM_TRMM ? (int)((long long)tm * PBM / BK) : 0;
+        const int half = bn / 2;
         const uint32_t bytes = 2u * (uint32_t)(C::A_BYTES + half * BK * 2);  // both CTAs' copies
         for (int kb = kb0; kb < nk; ++kb, ++g) {
           const int s = g % STAGES;
@@ -1153,7 +1211,7 @@ __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ desc
           uint8_t* sa = smem + s * C::STAGE_BYTES;
           const uint32_t fb = mapa_shared(&full[s], 0);
           tma_load_2d_pair(sa, &d.ta[0], fb, kb * BK, tm * PBM + (int)rank * BM);
-          tma_load_2d_pair(sa + C::A_BYTES, &d.tb[0], fb, kb * BK, tn * d.s.bn + (int)rank * half);
+          tma_load_2d_pair(sa + C::A_BYTES, &d.tb[0], fb, kb * BK, tn * bn + (int)rank * half);
         }
       }
       if (*abort && rank == 0) {  // every armed round (both CTAs' copies) lands before shared memory is released
@@ -1169,17 +1227,16 @@ __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ desc
       // ---------------- MMA issuer (leader) ----------------
       uint32_t g = 0, i = 0;
       bool issued = false;
+      TileAhead ta(descs, tiles, t_begin, t_end, 1);
       for (int t = t_begin; t < t_end; ++t, ++i) {
-        int p, tm, tn;
-        get_tile(descs, tiles, t, p, tm, tn);
-        const GemmDesc& d = descs[p];
-        const int nk = (d.s.K + BK - 1) / BK;
-        const int kb0 = first_kblock(d.s, tm * PBM, BK);
+        const TileMeta cur = ta.next();  // this tile's fields; the next tile's are requested here
+        const int nk = (int)((cur.K + BK - 1) / BK);
+        const int kb0 = cur.mode == PSGD_GEMM_TRMM ? (int)((long long)cur.tm * PBM / BK) : 0;
         const uint32_t acc = i & 1, aph = (i >> 1) & 1;
         if (!mbar_wait_for(&tempty[acc], aph ^ 1, abort, wait_ns)) break;
         tc_fence_after();
         const uint32_t dt = tmem_base + acc * BNMAX;
-        const uint32_t idesc = idesc_bf16_m256(d.s.bn);
+        const uint32_t idesc = idesc_bf16_m256(cur.bn);
         bool ok = true;
         for (int kb = kb0; kb < nk; ++kb, ++g) {
           const int s = g % STAGES;
