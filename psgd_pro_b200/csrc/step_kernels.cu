@@ -692,9 +692,10 @@ PSGD_DEVI void skew_issue(const PsgdSkewItem* __restrict__ items, const uint32_t
   }
 }
 
-// R1: the items carry the rank-one q update (u_hi != NULL); without it that code is compiled out, so the plain
-// kernel keeps its register count. Entries of a block are pipelined through SK_STAGES shared-memory stages
-// (cp.async): entry k + SK_STAGES is requested as soon as entry k's tiles have been read.
+// The element-wise form runs the 1-D factors (psgd_skew_rank1, R1 = true: the items carry the rank-one q update,
+// u_hi != NULL, applied to the staged tiles first); the 2-D factors take skew2_kernel below. Entries of a block are
+// pipelined through SK_STAGES shared-memory stages (cp.async): entry k + SK_STAGES is requested as soon as entry k's
+// tiles have been read.
 template <bool R1>
 __global__ void __launch_bounds__(256, 3) skew_kernel(const PsgdSkewItem* __restrict__ items,
                                                       const uint32_t* __restrict__ work, int nwork) {
