@@ -871,12 +871,33 @@ constexpr int SK2_SQ = SK * 17;                                    // one partia
 constexpr int SK2_SMEM = (SK2_STAGES * 2 * SK2_TILE + 2 * SK2_SQ) * (int)sizeof(float);
 PSGD_DEVI int sk2_off(int r, int chunk) { return r * SK + ((chunk ^ ((r >> 2) & 15)) << 2); }
 
-PSGD_DEVI void skew2_issue(const PsgdSkewItem* __restrict__ items, const uint32_t* __restrict__ work, int w,
-                           float* stage, int t) {
-  const PsgdSkewItem& it = items[work[2 * w]];
-  const int ti = work[2 * w + 1] >> 16, tj = work[2 * w + 1] & 0xFFFF;
-  const int n = it.n, i0 = ti * SK, j0 = tj * SK, nload = ti == tj ? 4 : 8;
-  const float* q = it.q;
+// The fields of a work entry the block needs (read one iteration ahead of use, so the dependent loads of the work
+// list and the item do not stall the block at the start of an entry).
+struct Sk2Meta {
+  const float* q;
+  void* r_hi;
+  void* r_lo;
+  float* part_row;
+  float* part_max;
+  float* part_dot;
+  long long ldr;
+  int n, ti, tj;
+};
+PSGD_DEVI Sk2Meta sk2_meta(const PsgdSkewItem* __restrict__ items, const uint32_t* __restrict__ work, int w,
+                           int nwork) {
+  Sk2Meta m{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 0, 0, 0, 0};
+  if (w < nwork) {
+    const uint32_t e = work[2 * w + 1];
+    const PsgdSkewItem& it = items[work[2 * w]];
+    m = Sk2Meta{it.q, it.r_hi, it.r_lo, it.part_row, it.part_max, it.part_dot, it.ldr, it.n, (int)(e >> 16),
+                (int)(e & 0xFFFF)};
+  }
+  return m;
+}
+
+PSGD_DEVI void skew2_issue(const Sk2Meta& m, float* stage, int t) {
+  const int n = m.n, i0 = m.ti * SK, j0 = m.tj * SK, nload = m.ti == m.tj ? 4 : 8;
+  const float* q = m.q;
   const int ch = t & 15, r0 = t >> 4;
   const bool vec = (n & 3) == 0 && (reinterpret_cast<uintptr_t>(q) & 15) == 0;
   for (int j = 0; j < nload; ++j) {
@@ -921,13 +942,16 @@ __global__ void __launch_bounds__(256, 2) skew2_kernel(const PsgdSkewItem* __res
   const int bi = t >> 4, bj = t & 15;
   int wnext = blockIdx.x;
   for (int st = 0; st < SK2_STAGES; ++st, wnext += gridDim.x) {
-    if (wnext < nwork) skew2_issue(items, work, wnext, sk2_smem + st * 2 * SK2_TILE, t);
+    if (wnext < nwork) skew2_issue(sk2_meta(items, work, wnext, nwork), sk2_smem + st * 2 * SK2_TILE, t);
     cp_async_commit();
   }
   int st = 0;
+  Sk2Meta it = sk2_meta(items, work, blockIdx.x, nwork);  // this entry's fields
   for (int w = blockIdx.x; w < nwork; w += gridDim.x, wnext += gridDim.x, st = st + 1 == SK2_STAGES ? 0 : st + 1) {
-    const PsgdSkewItem& it = items[work[2 * w]];
-    const int ti = work[2 * w + 1] >> 16, tj = work[2 * w + 1] & 0xFFFF;
+    // requested now, used at the end of this iteration (the entry refilling this stage) and in the next one
+    const Sk2Meta im = sk2_meta(items, work, wnext, nwork);
+    const Sk2Meta nm = sk2_meta(items, work, w + gridDim.x, nwork);
+    const int ti = it.ti, tj = it.tj;
     const int n = it.n, i0 = ti * SK, j0 = tj * SK;
     const bool diag = ti == tj;
     float* const sA = sk2_smem + st * 2 * SK2_TILE;
@@ -1068,8 +1092,9 @@ __global__ void __launch_bounds__(256, 2) skew2_kernel(const PsgdSkewItem* __res
       it.part_dot[(long long)(2 * ti) * tiles32 + 2 * tj] = dd;
     }
     __syncthreads();  // the stage, the partials and red are free: refill the stage with a later entry
-    if (wnext < nwork) skew2_issue(items, work, wnext, sA, t);
+    if (wnext < nwork) skew2_issue(im, sA, t);
     cp_async_commit();
+    it = nm;
   }
   cp_async_wait<0>();
 }
