@@ -827,6 +827,32 @@ PSGD_DEVI void get_tile(const GemmDesc* descs, const uint32_t* tiles, int t, int
   }
 }
 
+// Shared-memory descriptors of the issue loops: the 128-byte-swizzle descriptor of the stage ring's base, with a tile's
+// start address reached by adding its offset (in 16-byte units) to the low word. Every offset of the ring keeps the
+// start-address field below 2^14 (shared-memory addresses stay under 256 KB), so no carry leaves the field.
+struct DescBase {
+  uint32_t lo, hi;
+  PSGD_DEVI explicit DescBase(const void* base) {
+    const uint64_t d = sdesc_k_sw128(smem_u32(base));
+    lo = (uint32_t)d;
+    hi = (uint32_t)(d >> 32);
+  }
+  PSGD_DEVI uint64_t at(uint32_t byte_off) const { return ((uint64_t)hi << 32) | (lo + (byte_off >> 4)); }
+};
+
+// Position in the stage ring (stage index and the phase parity of its barriers), advanced once per K block.
+template <int STAGES>
+struct Ring {
+  int s = 0;
+  uint32_t ph = 0;
+  PSGD_DEVI void next() {
+    if (++s == STAGES) {
+      s = 0;
+      ph ^= 1;
+    }
+  }
+};
+
 // The fields of its tiles the producer and the MMA issuer need, requested one tile ahead (and the tile-list entry two tiles ahead),
 // so the global-memory latency of the next tile's metadata is hidden behind the current tile's MMAs instead of
 // idling the tensor pipe between tiles. (The loads stay where they are written: every mbarrier wait and MMA
@@ -939,7 +965,7 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
-      uint32_t g = 0;
+      Ring<STAGES> ring;
       uint32_t armed[STAGES];  // phases armed per stage, to drain in-flight copies on abort
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) armed[s] = 0;
@@ -952,9 +978,9 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
         const int nk = (int)((K + BK * C::KSUB - 1) / (BK * C::KSUB));
         const int kb0 = cur.mode == PSGD_GEMM_TRMM ? (int)((long long)tm * BM / (BK * C::KSUB)) : 0;
         const uint32_t sub_bytes = C::NOPS * (C::A_BYTES + bn * BK * 2);
-        for (int kb = kb0; kb < nk; ++kb, ++g) {
-          const int s = g % STAGES;
-          const uint32_t ph = (g / STAGES) & 1;
+        for (int kb = kb0; kb < nk; ++kb, ring.next()) {
+          const int s = ring.s;
+          const uint32_t ph = ring.ph;
           // 64-deep blocks of this stage that hold any of K (no copy is issued past the end)
           const int nsub = (int)min((long long)C::KSUB, (K - (long long)kb * BK * C::KSUB + BK - 1) / BK);
           if (!mbar_wait_for(&empty[s], ph ^ 1, abort, wait_ns)) break;
@@ -984,7 +1010,9 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      uint32_t g = 0, i = 0;
+      Ring<STAGES> ring;
+      const DescBase db(smem);
+      uint32_t i = 0;
       bool issued = false;
       TileAhead ta(descs, tiles, t_begin, t_end, t_step);
       for (int t = t_begin; t < t_end; t += t_step, ++i) {
@@ -999,25 +1027,24 @@ __device__ __forceinline__ void gemm_body(const GemmDesc* __restrict__ descs, co
         const uint32_t dt = tmem_base + acc * BNMAX;
         const uint32_t idesc = idesc_bf16_m128(bn);
         bool ok = true;
-        for (int kb = kb0; kb < nk; ++kb, ++g) {
-          const int s = g % STAGES;
-          const uint32_t ph = (g / STAGES) & 1;
-          if (!mbar_wait_for(&full[s], ph, abort, wait_ns)) {
+        for (int kb = kb0; kb < nk; ++kb, ring.next()) {
+          const int s = ring.s;
+          if (!mbar_wait_for(&full[s], ring.ph, abort, wait_ns)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const int nsub = (int)min((long long)C::KSUB, (K - (long long)kb * BK * C::KSUB + BK - 1) / BK);
           for (int j = 0; j < nsub; ++j) {
-            const uint32_t a_hi = smem_u32(smem + s * C::STAGE_BYTES + j * C::SUB_BYTES);
-            const uint32_t b_hi = a_hi + C::NOPS * C::A_BYTES;
+            const uint32_t a_off = (uint32_t)(s * C::STAGE_BYTES + j * C::SUB_BYTES);
+            const uint32_t b_off = a_off + C::NOPS * C::A_BYTES;
 #pragma unroll
             for (int kk = 0; kk < BK / 16; ++kk) {
-              const uint64_t ad = sdesc_k_sw128(a_hi + kk * 32), bd = sdesc_k_sw128(b_hi + kk * 32);
+              const uint64_t ad = db.at(a_off + kk * 32), bd = db.at(b_off + kk * 32);
               umma_bf16(dt, ad, bd, idesc, ((kb - kb0) | j | kk) != 0);
               if (SPLIT != 1) {
-                umma_bf16(dt, ad, sdesc_k_sw128(b_hi + C::B_BYTES + kk * 32), idesc, 1);
-                umma_bf16(dt, sdesc_k_sw128(a_hi + C::A_BYTES + kk * 32), bd, idesc, 1);
+                umma_bf16(dt, ad, db.at(b_off + C::B_BYTES + kk * 32), idesc, 1);
+                umma_bf16(dt, db.at(a_off + C::A_BYTES + kk * 32), bd, idesc, 1);
               }
             }
           }
@@ -1184,7 +1211,7 @@ __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ desc
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer (both CTAs) ----------------
-      uint32_t g = 0;
+      Ring<STAGES> ring;
       uint32_t armed[STAGES];  // rounds the leader armed per stage, drained on abort
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) armed[s] = 0;
@@ -1197,9 +1224,9 @@ __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ desc
         const int kb0 = cur.mode == PSGD_GEMM_TRMM ? (int)((long long)tm * PBM / BK) : 0;
         const int half = bn / 2;
         const uint32_t bytes = 2u * (uint32_t)(C::A_BYTES + half * BK * 2);  // both CTAs' copies
-        for (int kb = kb0; kb < nk; ++kb, ++g) {
-          const int s = g % STAGES;
-          const uint32_t ph = (g / STAGES) & 1;
+        for (int kb = kb0; kb < nk; ++kb, ring.next()) {
+          const int s = ring.s;
+          const uint32_t ph = ring.ph;
           if (!mbar_wait_for(&empty[s], ph ^ 1, abort, wait_ns)) break;
           if (rank == 0) {
             mbar_arrive_expect_tx(&full[s], bytes);
@@ -1225,7 +1252,9 @@ __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ desc
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
       // ---------------- MMA issuer (leader) ----------------
-      uint32_t g = 0, i = 0;
+      Ring<STAGES> ring;
+      const DescBase db(smem);
+      uint32_t i = 0;
       bool issued = false;
       TileAhead ta(descs, tiles, t_begin, t_end, 1);
       for (int t = t_begin; t < t_end; ++t, ++i) {
@@ -1238,19 +1267,18 @@ __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ desc
         const uint32_t dt = tmem_base + acc * BNMAX;
         const uint32_t idesc = idesc_bf16_m256(cur.bn);
         bool ok = true;
-        for (int kb = kb0; kb < nk; ++kb, ++g) {
-          const int s = g % STAGES;
-          const uint32_t ph = (g / STAGES) & 1;
-          if (!mbar_wait_for(&full[s], ph, abort, wait_ns)) {
+        for (int kb = kb0; kb < nk; ++kb, ring.next()) {
+          const int s = ring.s;
+          if (!mbar_wait_for(&full[s], ring.ph, abort, wait_ns)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(smem + s * C::STAGE_BYTES);
-          const uint32_t b0 = a0 + C::A_BYTES;
+          const uint32_t a_off = (uint32_t)(s * C::STAGE_BYTES);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
-            umma_bf16_pair(dt, sdesc_k_sw128(a0 + kk * 32), sdesc_k_sw128(b0 + kk * 32), idesc, ((kb - kb0) | kk) != 0);
+            umma_bf16_pair(dt, db.at(a_off + kk * 32), db.at(a_off + C::A_BYTES + kk * 32), idesc,
+                           ((kb - kb0) | kk) != 0);
           issued = true;
           umma_commit_pair(&empty[s], 3);
         }
