@@ -1137,11 +1137,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 //   empty[s] (both)     the leader's MMA commit, multicast to both CTAs, frees stage s;
 //   tfull[a] (both)     the leader's commit, multicast, hands accumulator a to both epilogues;
 //   tempty[a] (leader)  four epilogue warps of each CTA arrive (the peer's remotely) when accumulator a is drained.
+// A stage holds PAIR_KS consecutive 64-deep K blocks (sub-blocks of A_BYTES + B_BYTES each): every barrier round
+// and every wait of the MMA issuer covers 4 * PAIR_KS MMAs.
+constexpr int PAIR_BN = 256, PAIR_STAGES = 3, PAIR_KS = 2;
 template <int BNMAX, int STAGES>
 struct PairCfg {
+  static constexpr int KS = PAIR_KS;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = (BNMAX / 2) * BK * 2;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int SUB_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGE_BYTES = KS * SUB_BYTES;
   static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
   static constexpr int TMEM_COLS = 2 * BNMAX;
   static constexpr int CTRL_BYTES = 512;
@@ -1220,25 +1225,31 @@ __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ desc
         const TileMeta cur = ta.next();
         const GemmDesc& d = descs[cur.p];  // (only its tensor maps' addresses are taken below)
         const int tm = cur.tm, tn = cur.tn, bn = cur.bn;
-        const int nk = (int)((cur.K + BK - 1) / BK);
-        const int kb0 = cur.mode == PSGD_GEMM_TRMM ? (int)((long long)tm * PBM / BK) : 0;
+        const long long K = cur.K;
+        const int nk = (int)((K + BK * C::KS - 1) / (BK * C::KS));
+        const int kb0 = cur.mode == PSGD_GEMM_TRMM ? (int)((long long)tm * PBM / (BK * C::KS)) : 0;
         const int half = bn / 2;
-        const uint32_t bytes = 2u * (uint32_t)(C::A_BYTES + half * BK * 2);  // both CTAs' copies
+        const uint32_t sub_bytes = 2u * (uint32_t)(C::A_BYTES + half * BK * 2);  // both CTAs' copies
         for (int kb = kb0; kb < nk; ++kb, ring.next()) {
           const int s = ring.s;
           const uint32_t ph = ring.ph;
+          // 64-deep blocks of this stage that hold any of K (no copy is issued past the end)
+          const int nsub = (int)min((long long)C::KS, (K - (long long)kb * BK * C::KS + BK - 1) / BK);
           if (!mbar_wait_for(&empty[s], ph ^ 1, abort, wait_ns)) break;
           if (rank == 0) {
-            mbar_arrive_expect_tx(&full[s], bytes);
+            mbar_arrive_expect_tx(&full[s], sub_bytes * (uint32_t)nsub);
             armed[s] += 1;
             mbar_arrive_cluster_relaxed(mapa_shared(&go[s], 1));
           } else if (!mbar_wait_for(&go[s], ph, abort, wait_ns)) {
             break;
           }
-          uint8_t* sa = smem + s * C::STAGE_BYTES;
           const uint32_t fb = mapa_shared(&full[s], 0);
-          tma_load_2d_pair(sa, &d.ta[0], fb, kb * BK, tm * PBM + (int)rank * BM);
-          tma_load_2d_pair(sa + C::A_BYTES, &d.tb[0], fb, kb * BK, tn * bn + (int)rank * half);
+          for (int j = 0; j < nsub; ++j) {
+            uint8_t* sa = smem + s * C::STAGE_BYTES + j * C::SUB_BYTES;
+            const int x = (kb * C::KS + j) * BK;
+            tma_load_2d_pair(sa, &d.ta[0], fb, x, tm * PBM + (int)rank * BM);
+            tma_load_2d_pair(sa + C::A_BYTES, &d.tb[0], fb, x, tn * bn + (int)rank * half);
+          }
         }
       }
       if (*abort && rank == 0) {  // every armed round (both CTAs' copies) lands before shared memory is released
@@ -1259,8 +1270,9 @@ __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ desc
       TileAhead ta(descs, tiles, t_begin, t_end, 1);
       for (int t = t_begin; t < t_end; ++t, ++i) {
         const TileMeta cur = ta.next();  // this tile's fields; the next tile's are requested here
-        const int nk = (int)((cur.K + BK - 1) / BK);
-        const int kb0 = cur.mode == PSGD_GEMM_TRMM ? (int)((long long)cur.tm * PBM / BK) : 0;
+        const long long K = cur.K;
+        const int nk = (int)((K + BK * C::KS - 1) / (BK * C::KS));
+        const int kb0 = cur.mode == PSGD_GEMM_TRMM ? (int)((long long)cur.tm * PBM / (BK * C::KS)) : 0;
         const uint32_t acc = i & 1, aph = (i >> 1) & 1;
         if (!mbar_wait_for(&tempty[acc], aph ^ 1, abort, wait_ns)) break;
         tc_fence_after();
@@ -1274,11 +1286,16 @@ __device__ __forceinline__ void gemm_pair_body(const GemmDesc* __restrict__ desc
             break;
           }
           tc_fence_after();
-          const uint32_t a_off = (uint32_t)(s * C::STAGE_BYTES);
+          const int nsub = (int)min((long long)C::KS, (K - (long long)kb * BK * C::KS + BK - 1) / BK);
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            umma_bf16_pair(dt, db.at(a_off + kk * 32), db.at(a_off + C::A_BYTES + kk * 32), idesc,
-                           ((kb - kb0) | kk) != 0);
+          for (int j = 0; j < C::KS; ++j) {
+            if (j >= nsub) break;
+            const uint32_t a_off = (uint32_t)(s * C::STAGE_BYTES + j * C::SUB_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk)
+              umma_bf16_pair(dt, db.at(a_off + kk * 32), db.at(a_off + C::A_BYTES + kk * 32), idesc,
+                             ((kb - kb0) | j | kk) != 0);
+          }
           issued = true;
           umma_commit_pair(&empty[s], 3);
         }
@@ -1575,7 +1592,6 @@ static int launch_single(const GemmDesc& desc, const uint32_t* tiles, int ntiles
 }
 
 // ---- pair kernel launch: one cluster of two CTAs per segment of the tile list ----
-constexpr int PAIR_BN = 256, PAIR_STAGES = 6;
 constexpr int KIND_PAIR = 8;     // flag in the encoded kind: the group runs on the pair kernel
 constexpr int KIND_NARROW = 16;  // flag: every tile is at most 64 columns wide (one-CTA kernel, long K stages)
 

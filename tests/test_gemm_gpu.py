@@ -243,6 +243,46 @@ def test_pair_kernel_syrk_reductions(cuda, monkeypatch):
             assert abs(part_dot.double().sum().item() - want) <= 1e-4 * (ref.abs() * q.double().abs()).sum().item()
 
 
+def bf16_operand_from(x, dev):
+    hi, lo = K.operand(x.shape[0], x.shape[1], dev, split=False)
+    K.split_into(x.to(dev), hi, lo)
+    return x, (hi, lo)
+
+
+def test_pair_kernel_trmm(cuda, monkeypatch):
+    """TRMM mode on CTA pairs: C = triu(T) X. The operand holds zeros below the diagonal inside each tile's diagonal
+    band and NaN in the blocks left of it (columns before the tile's first row, 256-row tiles), which the K loop must
+    never read (K-block counts even and odd, pair tiles partial at the edge)."""
+    g = torch.Generator().manual_seed(37)
+    cases = [(512, 256), (1024, 512), (768, 512), (1000, 256)]
+    data = []
+    for n, p in cases:
+        T = torch.triu(torch.randn(n, n, generator=g) / n ** 0.5)
+        x = torch.randn(p, n, generator=g)  # X^T: the K-major operand of the product
+        i = torch.arange(n).view(n, 1)
+        j = torch.arange(n).view(1, n)
+        Tp = T.masked_fill(j < 256 * (i // 256), float("nan"))
+        (_, Top), (_, Xop) = bf16_operand_from(Tp, cuda), bf16_operand_from(x, cuda)
+        data.append((T, x, Top, Xop))
+
+    def build():
+        specs, outs, keep = [], [], []
+        for (n, p), (_, _, Top, Xop) in zip(cases, data):
+            out = torch.full((n, p), float("nan"), device=cuda)
+            keep += [Top, Xop]
+            specs.append(K.make_spec(Top, Xop, n, p, n, bn=256, mode=K.PSGD_GEMM_TRMM, out_f32=out))
+            outs.append(out)
+        return specs, outs, keep
+
+    pair = _pair_group(cuda, build, True, monkeypatch)
+    single = _pair_group(cuda, build, False, monkeypatch)
+    for (n, p), (Tu, x, Top, Xop), o, o1 in zip(cases, data, pair, single):
+        ref = Top[0][:, :n].float().nan_to_num(0.0).double() @ Xop[0][:, :n].double().T
+        assert torch.isfinite(o).all(), (n, p)
+        assert rel(o, ref) < 1e-5, (n, p)
+        assert rel(o, o1) < 1e-6
+
+
 def test_pair_kernel_aux_epilogue(cuda, monkeypatch):
     """The q-update form: Q <- beta Q + alpha (A B^T) with device scalars, Q^T stored as bf16."""
     g = torch.Generator().manual_seed(31)
