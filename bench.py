@@ -282,7 +282,7 @@ def roofline_of(inners, phase_ms, peaks, peak_src):
     achieved = flops / (tm * 1e-3) / 1e12
     peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
     kind = groups[dominant][0].kind
-    kernel = (f"gemm_pair_kernel<256,6,{kind & 7}>" if kind & 8 else
+    kernel = (f"gemm_pair_kernel<256,3,{kind & 7}>" if kind & 8 else
               (f"gemm_group_kernel<1,256,4,{kind}>" if inners[0]._split == 1 else
                f"gemm_group_kernel<3,128,3,{kind}>"))
     # DRAM traffic of the Procrustes pair-kernel launch, from one ncu capture (dram__bytes_read.sum +

@@ -397,7 +397,9 @@ class _Plan:
         self.nd_a = self._nd_chain(noisy=False)
         self.nd_t1 = nd_t1
         # the skinny rank-one products form groups of their own, so the big products' groups can run on CTA pairs
-        self.g_u1, self.g_u2, self.g_u3, self.g_u3r = self.group(u1), self.group(u2), self.group(u3), self.group(u3r)
+        # (and the 1 x n rows of 1-D parameters leave the Y products' groups for the same reason)
+        self.g_u1, self.g_u1r = self.group([x for x in u1 if x.M >= BM]), self.group([x for x in u1 if x.M < BM])
+        self.g_u2, self.g_u3, self.g_u3r = self.group(u2), self.group(u3), self.group(u3r)
 
         dense = [f for f in self.factors if f.kind == "dense"]
         nlb = [f for f in dense if not f.rank1]
@@ -518,7 +520,8 @@ class _Plan:
                 bn = choose_bn(n2, split)
                 p.apart = torch.zeros(cdiv(n1, BM) * cdiv(n2, bn), device=dev)
                 a2.append(self.spec(f1.P, p.gop, n1, n2, n1, bn=bn, out_f32=p.pg32, part_tile=p.apart))
-        self.g_a1, self.g_a2 = self.group(a1), self.group(a2)
+        self.g_a1, self.g_a1r = self.group([x for x in a1 if x.M >= BM]), self.group([x for x in a1 if x.M < BM])
+        self.g_a2 = self.group(a2)
         # A3: clip + apply
         ai, aw = [], []
         for k, p in enumerate(P):
@@ -709,6 +712,8 @@ class _Plan:
         self._run_nd(self.nd_u, self.nd_t1, tr, "nd")
         self._launch(self.g_u1)
         tr("u1")
+        self._launch(self.g_u1r)
+        tr("u1_r1")
         self._launch(self.g_u2)
         tr("u2")
         self._launch(self.g_u3)
@@ -761,6 +766,8 @@ class _Plan:
         self._run_nd(self.nd_a[0], self.nd_a[1], tr, "a_nd")
         self._launch(self.g_a1)
         tr("a1")
+        self._launch(self.g_a1r)
+        tr("a1_r1")
         self._launch(self.g_a2)
         tr("a2")
         check(L.psgd_apply(self.apply_dev.data_ptr(), self.apply_n, self.apply_work.data_ptr(), self.apply_nw, hy,
@@ -769,11 +776,13 @@ class _Plan:
 
     def phase_groups(self):
         """(name, GemmGroup) of every tensor-core phase, in the names run_update / run_apply trace."""
-        out = [("u1", self.g_u1), ("u2", self.g_u2), ("term1", self.g_u3), ("term1_r1", self.g_u3r)]
+        out = [("u1", self.g_u1), ("u1_r1", self.g_u1r), ("u2", self.g_u2), ("term1", self.g_u3),
+               ("term1_r1", self.g_u3r)]
         out += [(f"nlb_spd{k}", g) for k, g in enumerate(self.g_spd)]
         out += [("qupdate", self.g_u10)]
         out += [(f"nlb_skh{k}", g) for k, g in enumerate(self.g_skh)]
         out += [("S", self.g_u17), ("procrustes", self.g_u20), ("gram", self.g_u22), ("a1", self.g_a1),
+                ("a1_r1", self.g_a1r),
                 ("a2", self.g_a2)]
         out += [(f"nd_product{j}", g) for j, (_, g) in enumerate(self.nd_u)]
         out += [(f"a_nd_product{j}", g) for j, (_, g) in enumerate(self.nd_a[0])]
@@ -783,7 +792,7 @@ class _Plan:
         """Kernels of libpsgd_b200.so launched by one step (the RNG fill of the update uses torch's kernels)."""
         a_prep = self.prep_a_rest_n if (update and update_first and self.fuse_stage) else self.prep_a_n
         n = 2 + int(a_prep > 0)  # clip scale, apply, the apply's staging
-        groups = [self.g_a1, self.g_a2]
+        groups = [self.g_a1, self.g_a1r, self.g_a2]
         nd_perm = lambda stages, final: sum(int(p is not None and p[2] > 0) for p, _ in stages) + \
             int(final is not None and final[2] > 0)
         n += nd_perm(*self.nd_a)
@@ -796,7 +805,8 @@ class _Plan:
             n += 2 * int(self.fac_n > 0) + 2 * int(self.skf_n > 0)  # factor scalars: two launches each
             n += int(self.skew_n > 0) + int(self.skew1_n > 0) + int(self.rot_n > 0)  # skew (two kinds), rot
             n += int(self.trace_n > 0)  # trace of S o Q
-            groups += [self.g_u1, self.g_u2, self.g_u3, self.g_u3r, self.g_u10, self.g_u17, self.g_u20, self.g_u22]
+            groups += [self.g_u1, self.g_u1r, self.g_u2, self.g_u3, self.g_u3r, self.g_u10, self.g_u17, self.g_u20,
+                       self.g_u22]
             groups += self.g_spd + self.g_skh
         return n + sum(g is not None for g in groups)
 

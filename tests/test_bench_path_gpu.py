@@ -75,11 +75,13 @@ def test_benchmarked_path_matches_reference(cuda, precision):
     sc, opt, params, p0 = run(cuda, precision)
     tol = 2e-2 if precision == "bf16" else 1e-3
     if precision == "bf16":
-        # the long-reduction product groups run on the CTA-pair kernel, as in the benchmark (u1 and a1 hold the
-        # one-row products of the 1-D parameter, which keep their groups on the one-CTA kernel)
-        kinds = {name: g.kind for name, g in opt._plan.phase_groups()}
-        for name in ("u2", "term1", "qupdate", "S", "procrustes", "gram", "a2"):
+        # the long-reduction product groups run on the CTA-pair kernel, as in the benchmark (the one-row products of
+        # the 1-D parameter form groups of their own, u1_r1 / a1_r1 / term1_r1, on the one-CTA kernel)
+        kinds = {name: g.kind for name, g in opt._plan.phase_groups() if g is not None}
+        for name in ("u1", "u2", "term1", "qupdate", "S", "procrustes", "gram", "a1", "a2"):
             assert kinds[name] & PAIR, (name, kinds[name])
+        for name in ("u1_r1", "a1_r1"):
+            assert not kinds[name] & PAIR, (name, kinds[name])
     st = opt.state_dict()["state"]
     errs = {}
     for k, s in enumerate(st):
