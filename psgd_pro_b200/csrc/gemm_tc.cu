@@ -511,7 +511,9 @@ __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn,
   float* __restrict__ s_part_tile = sd.part_tile;
   float* __restrict__ s_part_col = sd.part_col;
   float* __restrict__ s_part_row = sd.part_row;
-  const float* __restrict__ s_dot = sd.dot_aux;
+  // (the fast kinds never carry a dot operand: SYRK problems with one take the general epilogue, which keeps the
+  // registers of the dot's loads out of the hot SYRK path)
+  const float* __restrict__ s_dot = nullptr;
   const long long s_ld_dot = sd.ld_dot;
   float* __restrict__ s_part_dot = sd.part_dot;
   float* __restrict__ s_diag_out = sd.diag_out;
@@ -547,7 +549,7 @@ __device__ __forceinline__ void epilogue_fast(const GemmDesc& d, int tm, int tn,
   float tsum = 0.f, dsum = 0.f;
   // The column-pass operand (aux, or the trace operand in SYRK mode) of the next chunk is requested while the
   // current one is processed.
-  const float* pre_src = KIND == EPI_AUX ? s_aux : (KIND == EPI_SYRK ? s_dot : nullptr);
+  const float* pre_src = KIND == EPI_AUX ? s_aux : nullptr;
   const long long pre_ld = KIND == EPI_AUX ? s_ld_aux : s_ld_dot;
   // The transposed pass reads the transformed values back from the staging block, except in SYRK mode where they
   // are alpha times the accumulator registers themselves.
@@ -1452,7 +1454,7 @@ static int fast_kind(const PsgdGemmSpec& s) {
   if (s.bn % 32 != 0) return EPI_GENERIC;
   if (!(f32_ok && b_ok && t_ok && aux_ok && dot_ok) || s.col_scale) return EPI_GENERIC;
   if (s.mode == PSGD_GEMM_SYRK) {
-    if (s.row_scale || s.aux || s.cs_mode || s.out_hi_t) return EPI_GENERIC;
+    if (s.row_scale || s.aux || s.cs_mode || s.out_hi_t || s.dot_aux) return EPI_GENERIC;
     if (s.out_packed)  // the packed triangle alone has its own fast path; with other outputs the general one
       return (s.out_f32 || s.out_hi || s.dot_aux || s.diag_out || s.part_row || s.part_tile) ? EPI_GENERIC : EPI_SYRKP;
     return EPI_SYRK;
