@@ -71,12 +71,44 @@ PSGD_DEVI uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {
   return c;
 }
 
+// The ten round keys of a key (k0, k1), formed once per thread: the generator's rounds then take them as operands
+// instead of bumping the key between rounds.
+struct PhiloxKeys {
+  uint32_t k0[10], k1[10];
+};
+PSGD_DEVI PhiloxKeys philox_keys(uint32_t k0, uint32_t k1) {
+  PhiloxKeys ks;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    ks.k0[r] = k0 + (uint32_t)r * 0x9E3779B9u;
+    ks.k1[r] = k1 + (uint32_t)r * 0xBB67AE85u;
+  }
+  return ks;
+}
+PSGD_DEVI uint4 philox4x32_10(uint4 c, const PhiloxKeys& ks) {
+  constexpr uint32_t M0 = 0xD2511F53u, M1 = 0xCD9E8D57u;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t hi0 = __umulhi(M0, c.x), lo0 = M0 * c.x;
+    const uint32_t hi1 = __umulhi(M1, c.z), lo1 = M1 * c.z;
+    c = make_uint4(hi1 ^ c.y ^ ks.k0[r], lo1, hi0 ^ c.w ^ ks.k1[r], lo0);
+  }
+  return c;
+}
+
 // Numbers 4 blk .. 4 blk + 3 of the sequence with key (k0, k1).
 PSGD_DEVI float unit_open(uint32_t w) {  // ((w >> 9) + 1/2) / 2^23, exactly: [1, 2) by its bits, minus 1 - 2^-24
   return __uint_as_float(0x3f800000u | (w >> 9)) - 0.99999994039535522f;
 }
+PSGD_DEVI float4 normal4_words(const uint4 w);
 PSGD_DEVI float4 normal4(unsigned long long blk, uint32_t k0, uint32_t k1) {
-  const uint4 w = philox4x32_10(make_uint4((uint32_t)blk, (uint32_t)(blk >> 32), 0u, 0u), k0, k1);
+  return normal4_words(philox4x32_10(make_uint4((uint32_t)blk, (uint32_t)(blk >> 32), 0u, 0u), k0, k1));
+}
+PSGD_DEVI float4 normal4(unsigned long long blk, const PhiloxKeys& ks) {
+  return normal4_words(philox4x32_10(make_uint4((uint32_t)blk, (uint32_t)(blk >> 32), 0u, 0u), ks));
+}
+// The four numbers of one generator output.
+PSGD_DEVI float4 normal4_words(const uint4 w) {
   const float u0 = unit_open(w.x), u1 = unit_open(w.y), u2 = unit_open(w.z), u3 = unit_open(w.w);
   // hardware approximations of log, reciprocal square root, sin and cos (errors near 1e-6, far below what damping
   // noise needs); -2 ln u > 0 for every u above; the angle 2 pi u - pi lies in (-pi, pi), where __sincosf is most
@@ -137,7 +169,7 @@ PSGD_DEVI void st8_split(void* out_hi, void* out_lo, long long o, const float* x
 // the whole batch before the conversions, and the new m is written back); otherwise `src` (g or m) is staged.
 template <bool BF16, bool EMA>
 PSGD_DEVI void prep_rows_vec8(const PsgdPrepItem& it, const void* gsrc, long long r0, int rows, float damping,
-                              bool gen, uint32_t k0, uint32_t k1, float mbeta, float malpha, uint4* stage) {
+                              bool gen, const PhiloxKeys& ks, float mbeta, float malpha, uint4* stage) {
   constexpr int PV = BF16 ? PREP_VEC : PREP_VEC / 2, CH = BF16 ? 1 : 2;  // vectors per batch, chunks per vector
   const int nvr = it.n2 >> 3, nvec = rows * nvr, t = threadIdx.x;
   const float inv_nvr = 1.f / (float)nvr;
@@ -210,7 +242,7 @@ PSGD_DEVI void prep_rows_vec8(const PsgdPrepItem& it, const void* gsrc, long lon
       if (it.xi) {
 #pragma unroll
         for (int hv = 0; hv < 2; ++hv) {
-          const float4 z = gen ? normal4((unsigned long long)(it.noise_base + idx) / 4 + hv, k0, k1)
+          const float4 z = gen ? normal4((unsigned long long)(it.noise_base + idx) / 4 + hv, ks)
                                : *reinterpret_cast<const float4*>(it.xi + idx + 4 * hv);
           const float zz[4] = {z.x, z.y, z.z, z.w};
 #pragma unroll
@@ -236,6 +268,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const PsgdPrepItem* __restric
   const float damping = hyper[PSGD_HY_DAMPING];
   const bool gen = hyper[PSGD_HY_NOISE] != 0.f;  // noise from the counter-based generator instead of xi
   const uint32_t k0 = __float_as_uint(hyper[PSGD_HY_NOISE_KEY0]), k1 = __float_as_uint(hyper[PSGD_HY_NOISE_KEY1]);
+  const PhiloxKeys ks = philox_keys(k0, k1);
   const float mbeta = hyper[PSGD_HY_MOM_BETA], malpha = hyper[PSGD_HY_MOM_ALPHA];
   const int ema_phase = (int)hyper[PSGD_HY_EMA_PHASE];
   for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
@@ -257,14 +290,14 @@ __global__ void __launch_bounds__(256) prep_kernel(const PsgdPrepItem* __restric
       if (vec) {
         if (MOM && ema) {
           if (it.g_bf16)
-            prep_rows_vec8<true, true>(it, src, r0, rows, damping, gen, k0, k1, mbeta, malpha, prep_stage);
+            prep_rows_vec8<true, true>(it, src, r0, rows, damping, gen, ks, mbeta, malpha, prep_stage);
           else
-            prep_rows_vec8<false, true>(it, src, r0, rows, damping, gen, k0, k1, mbeta, malpha, prep_stage);
+            prep_rows_vec8<false, true>(it, src, r0, rows, damping, gen, ks, mbeta, malpha, prep_stage);
         } else {
           if (it.g_bf16)
-            prep_rows_vec8<true, false>(it, src, r0, rows, damping, gen, k0, k1, mbeta, malpha, prep_stage);
+            prep_rows_vec8<true, false>(it, src, r0, rows, damping, gen, ks, mbeta, malpha, prep_stage);
           else
-            prep_rows_vec8<false, false>(it, src, r0, rows, damping, gen, k0, k1, mbeta, malpha, prep_stage);
+            prep_rows_vec8<false, false>(it, src, r0, rows, damping, gen, ks, mbeta, malpha, prep_stage);
         }
       } else {
         for (int k = threadIdx.x; k < rows * it.n2; k += blockDim.x) {
