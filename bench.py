@@ -289,7 +289,7 @@ def roofline_of(inners, phase_ms, peaks, peak_src):
     # dram__bytes_write.sum) of the one-layer Llama case (the same factor sizes), scaled to this launch by FLOPs
     traffic = None
     if dominant in ("procrustes", "qupdate") and kind == 9:
-        traffic = flops * (2.6948e9 / 1.2609e12)
+        traffic = flops * (2.663e9 / 1.2609e12)
     return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
             "traffic": traffic, "traffic_unit": "bytes per launch", "kernel": kernel, "phase": dominant,
             "flops_per_launch": flops, "ms_per_launch": tm,
