@@ -210,7 +210,11 @@ def test_pair_kernel_plain_and_transposed(cuda, monkeypatch):
         assert rel(t[:, :M].float(), ref.T) < 1e-2
 
 
-def test_pair_kernel_syrk_reductions(cuda, monkeypatch):
+@pytest.mark.parametrize("dot", [True, False])
+def test_pair_kernel_syrk_reductions(cuda, monkeypatch, dot):
+    """SYRK on CTA pairs and on one CTA: fp32 and bf16 outputs (both triangles, the mirror through TMA stores on
+    pairs), row sums of squares and the diagonal; with the trace operand (dot) the tiles take the general epilogue,
+    without it the fast one."""
     g = torch.Generator().manual_seed(29)
     cases = [(512, 96), (768, 300), (1280, 64), (2048, 512)]
     data = [bf16_operand(n, Kd, cuda, g) for n, Kd in cases]
@@ -226,21 +230,27 @@ def test_pair_kernel_syrk_reductions(cuda, monkeypatch):
             diag = torch.empty(n, device=cuda)
             part_dot = torch.zeros(Tm * Tn, device=cuda)
             keep += [X, hi]
+            extra = dict(dot_aux=q, part_dot=part_dot) if dot else {}
             specs.append(K.make_spec(X, X, n, n, Kd, bn=256, mode=K.PSGD_GEMM_SYRK, out_f32=out, out_hi=hi[0],
-                                     part_row=part_row, diag_out=diag, dot_aux=q, part_dot=part_dot))
-            outs.append((out, part_row, diag, part_dot))
+                                     part_row=part_row, diag_out=diag, **extra))
+            outs.append((out, hi[0], part_row, diag, part_dot))
         return specs, outs, keep
 
     for pair in (True, False):
-        for (n, Kd), (x, X), q, (out, part_row, diag, part_dot) in zip(cases, data, qs,
-                                                                      _pair_group(cuda, build, pair, monkeypatch)):
+        for (n, Kd), (x, X), q, (out, hi, part_row, diag, part_dot) in zip(
+                cases, data, qs, _pair_group(cuda, build, pair, monkeypatch)):
             ref = X[0][:, :Kd].double() @ X[0][:, :Kd].double().T
             assert torch.equal(out, out.T), (n, pair)
             assert rel(out, ref) < 1e-5
+            h = hi[:, :n]
+            assert torch.equal(h, h.T), (n, pair)
+            assert rel(h.float(), ref) < 1e-2
             assert rel(part_row.sum(0), (ref ** 2).sum(1)) < 1e-4
             assert rel(diag, ref.diagonal()) < 2e-5
-            want = (ref * q.double()).sum().item()
-            assert abs(part_dot.double().sum().item() - want) <= 1e-4 * (ref.abs() * q.double().abs()).sum().item()
+            if dot:
+                want = (ref * q.double()).sum().item()
+                assert abs(part_dot.double().sum().item() - want) <= \
+                    1e-4 * (ref.abs() * q.double().abs()).sum().item()
 
 
 def bf16_operand_from(x, dev):
