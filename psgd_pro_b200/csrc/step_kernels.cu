@@ -897,11 +897,13 @@ __global__ void __launch_bounds__(256, 3) skew_kernel(const PsgdSkewItem* __rest
 // keep 256-byte rows with their 16-byte chunks permuted (chunk c of row r at position c ^ ((r / 4) mod 16)), which
 // makes the cp.async writes, the row reads of A and the block reads of B all free of bank conflicts. Row sums of
 // squares go through shared memory (partials per 4-column block, summed in a fixed order). Entries are pipelined
-// through SK2_STAGES stages; two blocks share an SM.
+// through SK2_STAGES stages; two blocks share an SM. D's rows leave straight from the registers (16 lanes write one
+// 128-byte row); the mirror's rows are spread over all warps, so it passes through an 8 KB block (MIR) first.
 constexpr int SK2_STAGES = 3;
 constexpr int SK2_TILE = SK * SK;                                  // floats per staged tile
 constexpr int SK2_SQ = SK * 17;                                    // one partial array: 64 rows x 16 (+1 pad)
-constexpr int SK2_SMEM = (SK2_STAGES * 2 * SK2_TILE + 2 * SK2_SQ) * (int)sizeof(float);
+constexpr int SK2_MIR = SK * SK * 2;                               // bytes: one bf16 64 x 64 tile
+constexpr int SK2_SMEM = (SK2_STAGES * 2 * SK2_TILE + 2 * SK2_SQ) * (int)sizeof(float) + SK2_MIR;
 PSGD_DEVI int sk2_off(int r, int chunk) { return r * SK + ((chunk ^ ((r >> 2) & 15)) << 2); }
 
 // The fields of a work entry the block needs (read one iteration ahead of use, so the dependent loads of the work
@@ -950,10 +952,9 @@ PSGD_DEVI void skew2_issue(const Sk2Meta& m, float* stage, int t) {
   }
 }
 
-// Output staging (interior pairs with 16-byte aligned rows): once every thread holds its block in registers, the
-// stage's tiles are dead, and the bf16 results are written into that space (hi D, hi -D^T, then lo D, lo -D^T in
-// fp32 mode: 8 KB each, 128-byte rows of sixteen 8-byte units, unit u of row r at u ^ ((r / 4) mod 16), free of
-// bank conflicts for both the block writes and the row reads) and leave in 16-byte row chunks.
+// Mirror staging (interior pairs with 16-byte aligned rows): the bf16 mirror -D^T is written into MIR (128-byte rows
+// of sixteen 8-byte units, unit u of row r at u ^ ((r / 4) mod 16), free of bank conflicts for both the block writes
+// and the row reads) and leaves in 16-byte row chunks; in fp32 mode its lo half takes a second round through MIR.
 PSGD_DEVI int sk2_unit(int r, int u) { return r * 16 + (u ^ ((r >> 2) & 15)); }  // in 8-byte units
 
 PSGD_DEVI uint2 pack4_bf16(const float* x) {
@@ -965,11 +966,24 @@ PSGD_DEVI void lo4(const float* x, float* lo) {  // x - bf16(x), as the split st
   for (int i = 0; i < 4; ++i) lo[i] = x[i] - __bfloat162float(__float2bfloat16_rn(x[i]));
 }
 
+// Writes rows R = t / 8 and t / 8 + 32 of the 64 x 64 bf16 tile held in MIR, 16 bytes (chunk t % 8) each.
+PSGD_DEVI void sk2_mirror_out(const uint8_t* mir, __nv_bfloat16* dst, long long ld, int row0, int col0, int t) {
+  const int k = t & 7;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int R = (t >> 3) + 32 * h, f = (R >> 2) & 15;
+    uint4 v = reinterpret_cast<const uint4*>(mir)[R * 8 + (k ^ (f >> 1))];
+    if (f & 1) v = make_uint4(v.z, v.w, v.x, v.y);
+    *reinterpret_cast<uint4*>(dst + (long long)(row0 + R) * ld + col0 + 8 * k) = v;
+  }
+}
+
 __global__ void __launch_bounds__(256, 2) skew2_kernel(const PsgdSkewItem* __restrict__ items,
                                                        const uint32_t* __restrict__ work, int nwork) {
   extern __shared__ __align__(16) float sk2_smem[];
   float* const sq0 = sk2_smem + SK2_STAGES * 2 * SK2_TILE;  // [row of D][bj]: row sums over 4-column blocks
   float* const sq1 = sq0 + SK2_SQ;                          // [row of -D^T][bi]
+  uint8_t* const mir = reinterpret_cast<uint8_t*>(sq1 + SK2_SQ);
   __shared__ float red[8][2];
   const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
   const int bi = t >> 4, bj = t & 15;
@@ -981,7 +995,7 @@ __global__ void __launch_bounds__(256, 2) skew2_kernel(const PsgdSkewItem* __res
   int st = 0;
   Sk2Meta it = sk2_meta(items, work, blockIdx.x, nwork);  // this entry's fields
   for (int w = blockIdx.x; w < nwork; w += gridDim.x, wnext += gridDim.x, st = st + 1 == SK2_STAGES ? 0 : st + 1) {
-    // requested now, used at the end of this iteration (the entry refilling this stage) and in the next one
+    // requested now, used after the entry's barrier (the entry refilling this stage) and in the next iteration
     const Sk2Meta im = sk2_meta(items, work, wnext, nwork);
     const Sk2Meta nm = sk2_meta(items, work, w + gridDim.x, nwork);
     const int ti = it.ti, tj = it.tj;
@@ -989,7 +1003,9 @@ __global__ void __launch_bounds__(256, 2) skew2_kernel(const PsgdSkewItem* __res
     const bool diag = ti == tj;
     float* const sA = sk2_smem + st * 2 * SK2_TILE;
     const float* const sB = diag ? sA : sA + SK2_TILE;
-    cp_async_wait<SK2_STAGES - 1>();  // this entry's group is complete (later groups may still be in flight)
+    // this entry's group is complete (later groups may still be in flight); the previous entry's reads of MIR, the
+    // partials and red are done
+    cp_async_wait<SK2_STAGES - 1>();
     __syncthreads();
     float d[4][4];  // d[r][c] = A[4 bi + r][4 bj + c] - B[4 bj + c][4 bi + r]
     {
@@ -1037,70 +1053,53 @@ __global__ void __launch_bounds__(256, 2) skew2_kernel(const PsgdSkewItem* __res
       red[wid][1] = dsum;
     }
     const bool lo = it.r_lo != nullptr;
-    // Rn[TI, TJ] rows i0 + 4 bi + r, columns j0 + 4 bj ..; Rn[TJ, TI] rows j0 + 4 bj + c, columns i0 + 4 bi ..
-    const bool staged = i0 + SK <= n && j0 + SK <= n && (it.ldr % 8) == 0 &&
-                        (reinterpret_cast<uintptr_t>(it.r_hi) & 15) == 0 &&
-                        (reinterpret_cast<uintptr_t>(it.r_lo) & 15) == 0;
-    __syncthreads();  // the stage's tiles are dead: reuse it for the outputs; partials and red are complete
-    if (staged) {
-      uint2* const ou = reinterpret_cast<uint2*>(sA);  // four 8 KB tiles of 1024 units
+    // Rn[TI, TJ] rows i0 + 4 bi + r, columns j0 + 4 bj .. (16 lanes cover one 128-byte row)
+    const bool full = i0 + SK <= n && j0 + SK <= n;
+    {
+      const int col = j0 + 4 * bj, nv = full ? 4 : max(0, min(4, n - col));
+      const bool vs = nv == 4 && (it.ldr % 4) == 0;
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
-        ou[sk2_unit(4 * bi + r, bj)] = pack4_bf16(d[r]);
-        if (lo) {
+        const int row = i0 + 4 * bi + r;
+        if (full || (row < n && nv > 0)) st4_split(it.r_hi, it.r_lo, (long long)row * it.ldr + col, d[r], vs, nv);
+      }
+    }
+    // Rn[TJ, TI] rows j0 + 4 bj + c, columns i0 + 4 bi ..: through MIR when the rows take 16-byte chunks
+    const bool staged = !diag && full && (it.ldr % 8) == 0 && (reinterpret_cast<uintptr_t>(it.r_hi) & 15) == 0 &&
+                        (reinterpret_cast<uintptr_t>(it.r_lo) & 15) == 0;
+    uint2* const mu = reinterpret_cast<uint2*>(mir);
+    if (staged) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float m[4] = {-d[0][c], -d[1][c], -d[2][c], -d[3][c]};
+        mu[sk2_unit(4 * bj + c, bi)] = pack4_bf16(m);
+      }
+    } else if (!diag) {
+      const int col = i0 + 4 * bi, nv = max(0, min(4, n - col));
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int row = j0 + 4 * bj + c;
+        const float m[4] = {-d[0][c], -d[1][c], -d[2][c], -d[3][c]};
+        if (row < n && nv > 0)
+          st4_split(it.r_hi, it.r_lo, (long long)row * it.ldr + col, m, nv == 4 && (it.ldr % 4) == 0, nv);
+      }
+    }
+    __syncthreads();  // the stage's tiles are dead; MIR, the partials and red are complete
+    if (wnext < nwork) skew2_issue(im, sA, t);  // refill the stage with a later entry
+    cp_async_commit();
+    if (staged) {
+      sk2_mirror_out(mir, reinterpret_cast<__nv_bfloat16*>(it.r_hi), it.ldr, j0, i0, t);
+      if (lo) {  // second round through MIR for the lo half
+        __syncthreads();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float m[4] = {-d[0][c], -d[1][c], -d[2][c], -d[3][c]};
           float l[4];
-          lo4(d[r], l);
-          ou[2048 + sk2_unit(4 * bi + r, bj)] = pack4_bf16(l);
+          lo4(m, l);
+          mu[sk2_unit(4 * bj + c, bi)] = pack4_bf16(l);
         }
-      }
-      if (!diag) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const float m[4] = {-d[0][c], -d[1][c], -d[2][c], -d[3][c]};
-          ou[1024 + sk2_unit(4 * bj + c, bi)] = pack4_bf16(m);
-          if (lo) {
-            float l[4];
-            lo4(m, l);
-            ou[3072 + sk2_unit(4 * bj + c, bi)] = pack4_bf16(l);
-          }
-        }
-      }
-      __syncthreads();
-      // 16-byte row chunks: thread t takes chunk t % 8 of rows t / 8 and t / 8 + 32 of each tile it writes
-      const int k = t & 7;
-#pragma unroll
-      for (int o = 0; o < 4; ++o) {
-        if ((o & 1) && diag) continue;
-        if ((o & 2) && !lo) continue;
-        const int row0 = (o & 1) ? j0 : i0, col0 = (o & 1) ? i0 : j0;
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>((o & 2) ? it.r_lo : it.r_hi);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int R = (t >> 3) + 32 * h, f = (R >> 2) & 15;
-          uint4 v = reinterpret_cast<const uint4*>(sA)[o * 512 + R * 8 + (k ^ (f >> 1))];
-          if (f & 1) v = make_uint4(v.z, v.w, v.x, v.y);
-          *reinterpret_cast<uint4*>(dst + (long long)(row0 + R) * it.ldr + col0 + 8 * k) = v;
-        }
-      }
-    } else {
-      {
-        const int col = j0 + 4 * bj, nv = max(0, min(4, n - col));
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          const int row = i0 + 4 * bi + r;
-          if (row < n && nv > 0)
-            st4_split(it.r_hi, it.r_lo, (long long)row * it.ldr + col, d[r], nv == 4 && (it.ldr % 4) == 0, nv);
-        }
-      }
-      if (!diag) {
-        const int col = i0 + 4 * bi, nv = max(0, min(4, n - col));
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int row = j0 + 4 * bj + c;
-          const float m[4] = {-d[0][c], -d[1][c], -d[2][c], -d[3][c]};
-          if (row < n && nv > 0)
-            st4_split(it.r_hi, it.r_lo, (long long)row * it.ldr + col, m, nv == 4 && (it.ldr % 4) == 0, nv);
-        }
+        __syncthreads();
+        sk2_mirror_out(mir, reinterpret_cast<__nv_bfloat16*>(it.r_lo), it.ldr, j0, i0, t);
       }
     }
     if (t < 2 * SK) {  // row sums: threads 0..63 the rows of Rn[TI, TJ], 64..127 those of Rn[TJ, TI]
@@ -1124,9 +1123,6 @@ __global__ void __launch_bounds__(256, 2) skew2_kernel(const PsgdSkewItem* __res
       it.part_max[(long long)(2 * ti) * tiles32 + 2 * tj] = m;
       it.part_dot[(long long)(2 * ti) * tiles32 + 2 * tj] = dd;
     }
-    __syncthreads();  // the stage, the partials and red are free: refill the stage with a later entry
-    if (wnext < nwork) skew2_issue(im, sA, t);
-    cp_async_commit();
     it = nm;
   }
   cp_async_wait<0>();
