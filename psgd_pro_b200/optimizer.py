@@ -634,8 +634,10 @@ class _Plan:
         tr(f"{tag}_permute_out")
 
     def _nlb_prep(self, fs, skew):
+        """One item (one CTA) per factor, the largest factors first: the items are independent, and starting the
+        longest CTAs in the first wave shortens the launch's tail."""
         items = []
-        for f in fs:
+        for f in sorted(fs, key=lambda f: -f.n):
             it = _capi.NlbPrepItem()
             A = f.R if skew else f.T
             it.a_hi, it.a_lo, it.lda, it.n, it.skew = K.ptr(A[0]), K.ptr(A[1]), A[0].stride(0), f.n, int(skew)
